@@ -1,0 +1,577 @@
+#!/usr/bin/env python
+"""Benchmark of the GQA attention hot path on B200.
+
+One step = one pass of the hot path over one batch of synthetic input that
+is already resident in HBM.  Workloads (--workload):
+
+  llama3_decode (default)  Llama-3-8B-shaped decode: 32 sequences x 8192
+                           cached positions per GPU, 32 q / 8 kv heads,
+                           d=128, bf16 KV, f32 q/out.  Metric: HBM GB/s of
+                           algorithmic bytes (K+V read once, q read, out
+                           written).  N GPUs = N independent batches
+                           ("weak": sequences shard with no collective).
+  batched_tinyllama        64 ragged sequences (U[128,4096], f16 KV,
+                           TinyLlama heads) sharded over the GPUs by
+                           longest-processing-time ("strong").
+  longctx                  one 131072-position sequence (Llama-3 heads,
+                           bf16) split along its KV length over the GPUs;
+                           per-GPU (m, l, o) partials all-gathered over
+                           NCCL and merged ("strong").
+  llama3_prefill           causal prefill 4 x 8192, 32/8 heads, d=128,
+                           bf16 operands (TFLOP/s of 4*d*H*causal pairs).
+
+The default decode line also carries a "prefill" object measured in the
+same run on the llama3_prefill workload.
+
+--impl reference times the CPU restatement of the reference's attention
+(oracle/, the reference is Rust and cannot be built here) on the host cores
+over a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+DECODE_METRIC = "GQA decode-attn HBM GB/s (% peak) + prefill TFLOP/s"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name: str):
+    """traffic_bytes_per_launch recorded from an ncu capture in profiles/."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, torch_index: int):
+        self.proc = None
+        try:
+            import torch
+            p = torch.cuda.get_device_properties(torch_index)
+            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", bus], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception as e:  # no nvidia-smi: report no clocks
+            log("clock sampler unavailable:", e)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+class Dist:
+    def __init__(self, n_gpus: int):
+        import torch
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != n_gpus:
+            raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={self.world}")
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+        else:
+            torch.cuda.set_device(0)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        self.pg.all_reduce(t)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def timed_loop(fn, steps: int, warmup: int, dist: Dist, sampler_index: int):
+    """W untimed steps, then K steps bracketed by barrier + synchronize, timed
+    with CUDA events on the launching stream; max over ranks."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    sampler = ClockSampler(sampler_index)
+    time.sleep(0.25)  # let the sampler start before the timed region
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    dist.barrier()
+    ms = start.elapsed_time(end)
+    return dist.max(ms), clocks
+
+
+def kernel_ms(fn, reps: int = 30) -> float:
+    """Average device duration of one launch of fn (events around each)."""
+    import torch
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in ev:
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev) / reps
+
+
+# ---------------------------------------------------------------------------
+# workloads on the device
+# ---------------------------------------------------------------------------
+def gen_normal(shape, dtype, device, gen):
+    import torch
+    return torch.randn(shape, generator=gen, device=device, dtype=torch.float32).to(dtype)
+
+
+def build_llama3_decode(dev, seed, n_seqs=32, length=8192):
+    import torch
+
+    import bml_b200
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    H, Hkv, d = 32, 8, 128
+    ks = [gen_normal((length, Hkv, d), torch.bfloat16, dev, gen) for _ in range(n_seqs)]
+    vs = [gen_normal((length, Hkv, d), torch.bfloat16, dev, gen) for _ in range(n_seqs)]
+    q = gen_normal((n_seqs, H, d), torch.float32, dev, gen)
+    batch = bml_b200.SeqBatch(ks, vs)
+    return q, batch, H
+
+
+def build_batched_tinyllama(dev, rank, world):
+    import numpy as np
+    import torch
+
+    import bml_b200
+    from bml_b200 import sharding
+    from bml_b200 import workloads as W
+    lens = W.batched_lengths()
+    mine = sharding.lpt_partition([int(x) for x in lens], world)[rank]
+    gen = torch.Generator(device=dev).manual_seed(2 + 1000 * rank)
+    H, Hkv, d = 32, 4, 64
+    ks = [gen_normal((int(lens[i]), Hkv, d), torch.float16, dev, gen) for i in mine]
+    vs = [gen_normal((int(lens[i]), Hkv, d), torch.float16, dev, gen) for i in mine]
+    q = gen_normal((len(mine), H, d), torch.float32, dev, gen)
+    return q, bml_b200.SeqBatch(ks, vs), H, int(np.sum(lens))
+
+
+def decode_step_bytes(batch, n_heads):
+    return batch.kv_bytes + len(batch) * n_heads * batch.head_dim * 8
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle) on a bounded sample
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(workload: str, budget_s: float):
+    """Times the oracle (all host threads) on a bounded sample of the
+    workload; returns (GB/s, threads, description)."""
+    import numpy as np
+
+    import oracle
+    from bml_b200 import workloads as W
+    threads = oracle.num_threads()
+    if workload == "batched_tinyllama":
+        q, ks, vs = W.batched_tinyllama(n_seqs=8)
+        code, nkv, d, es = None, 4, 64, 2
+        desc = "first 8 of the 64 ragged f16 sequences (seed 2)"
+    elif workload == "longctx":
+        q1, k, v = W.longctx_decode(length=16384)
+        q, ks, vs = q1[None], [k], [v]
+        code, nkv, d, es = oracle.BF16, 8, 128, 2
+        desc = "first 16384 of 131072 positions (seed 4)"
+    else:
+        q, k, v = W.llama3_decode(n_seqs=2)
+        ks, vs = list(k), list(v)
+        code, nkv, d, es = oracle.BF16, 8, 128, 2
+        desc = "2 of the 32 sequences x 8192 positions (seed 3)"
+    n_heads = q.shape[1]
+    total = sum(x.shape[0] for x in ks)
+    nbytes = W.decode_bytes(total, nkv, d, es, len(ks), n_heads)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.attn_decode_batched(q, ks, vs, dtype=code, n_threads=threads)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return nbytes / dt / 1e9, threads, f"{desc}, {reps} passes, {dt * 1e3:.1f} ms/pass"
+
+
+def cpu_prefill_sample(budget_s: float):
+    """Oracle on the last 16 query rows of one head group... of the 4x8192
+    prefill; returns TFLOP/s (causal pairs actually computed)."""
+    import oracle
+    from bml_b200 import workloads as W
+    threads = oracle.num_threads()
+    S = 8192
+    q, k, v = W.llama3_prefill(n_seqs=1, seq_len=S)
+    rows = (S - 16, S)
+    pairs = sum(t + 1 for t in range(*rows))
+    flops = 4 * 128 * 32 * pairs
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.attn_prefill(W.bf16_bits_to_f32(q), k, v, dtype=oracle.BF16, rows=rows, n_threads=threads)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return flops / dt / 1e12, threads, f"query rows {rows[0]}..{rows[1] - 1} of one 8192-token sequence, all 32 heads, {reps} passes"
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+def run_prefill(dev, steps, warmup, dist, peaks):
+    import torch
+
+    import bml_b200
+    from bml_b200 import workloads as W
+    gen = torch.Generator(device=dev).manual_seed(3 + 1000 * dist.rank)
+    n, S, H, Hkv, d = 4, 8192, 32, 8, 128
+    q = gen_normal((n, S, H, d), torch.bfloat16, dev, gen)
+    k = gen_normal((n, S, Hkv, d), torch.bfloat16, dev, gen)
+    v = gen_normal((n, S, Hkv, d), torch.bfloat16, dev, gen)
+    out = torch.empty(n, S, H, d, dtype=torch.float32, device=dev)
+    fn = lambda: bml_b200.prefill(q, k, v, out=out)  # noqa: E731
+    try:
+        fn()
+        torch.cuda.synchronize()
+    except bml_b200.BmlUnsupported as e:
+        return {"unavailable": str(e)}
+    ms, clocks = timed_loop(fn, steps, warmup, dist, dist.local)
+    flops = W.prefill_flops(n, S, H, d)
+    tflops = dist.world * flops * steps / (ms * 1e-3) / 1e12
+    kms = kernel_ms(fn, 10)
+    ach = flops / (kms * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    return {"metric": "causal prefill TFLOP/s", "value": round(tflops, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(ms / steps, 4), "steps": steps,
+            "config": {"workload": "llama3_prefill", "n_seqs": n, "seq_len": S, "n_heads": H,
+                       "n_kv_heads": Hkv, "head_dim": d, "causal": True, "dtype": "bf16"},
+            "roofline": {"bound": "tensor", "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(ach / peak, 4),
+                         "traffic": profile_traffic("prefill_tcgen05_llama3.txt")},
+            "clocks": clocks}
+
+
+def run_b200(args):
+    import torch
+
+    import bml_b200
+    dist = Dist(args.gpus)
+    dev = dist.device
+    peaks, peak_kind = load_peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    res = {"n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+           "vs_baseline": None, "data": "synthetic: seeded N(0,1) on the device (torch generator)",
+           "peak_source": f"{peak_kind} ({PEAKS_PATH if peak_kind == 'measured' else 'fallback'})"}
+    wl = args.workload
+    if wl == "llama3_prefill":
+        pre = run_prefill(dev, args.steps, args.warmup, dist, peaks)
+        res.update(pre)
+        res.update({"metric": DECODE_METRIC, "dtype": "bf16", "scaling": "weak", "gpu_launches": args.steps})
+        emit(res, dist)
+        return
+    if wl == "llama3_decode":
+        q, batch, H = build_llama3_decode(dev, 3 + 1000 * dist.rank)
+        scaling = "weak"
+        cfg = {"workload": "llama3_decode", "n_seqs_per_gpu": len(batch), "context": 8192, "n_heads": H,
+               "n_kv_heads": 8, "head_dim": 128, "kv_dtype": "bf16",
+               "l2": "inputs larger than L2 (1 GiB of KV per step vs 126 MB)"}
+        dtype = "f32 (bf16 KV)"
+    elif wl == "batched_tinyllama":
+        q, batch, H, _ = build_batched_tinyllama(dev, dist.rank, dist.world)
+        scaling = "strong"
+        cfg = {"workload": "batched_tinyllama", "n_seqs": 64, "lengths": "U[128,4096] seed 2",
+               "n_heads": H, "n_kv_heads": 4, "head_dim": 64, "kv_dtype": "f16",
+               "sharding": "LPT over GPUs, no collective",
+               "l2": "147 MB of KV per step > 126 MB L2"}
+        dtype = "f32 (f16 KV)"
+    elif wl == "longctx":
+        return run_longctx(args, dist, peaks, res)
+    else:
+        raise SystemExit(f"unknown workload {wl}")
+
+    ws = bml_b200.Workspace(dev).ensure(len(batch), H, batch.head_dim)
+    out = torch.empty_like(q)
+    fn = lambda: bml_b200.decode_batched(q, batch, out=out, workspace=ws)  # noqa: E731
+    fn()
+    torch.cuda.synchronize()
+    ms, clocks = timed_loop(fn, args.steps, args.warmup, dist, dist.local)
+    step_bytes = decode_step_bytes(batch, H)
+    total_bytes = dist.sum(step_bytes)
+    gbs = total_bytes * args.steps / (ms * 1e-3) / 1e9
+    kms = kernel_ms(fn)
+    ach = step_bytes / (kms * 1e-3) / 1e9
+    ws.check()
+
+    # end to end through the public API with host buffers
+    e2e = e2e_decode(q, batch, ws, args, dist, step_bytes)
+
+    res.update({
+        "metric": DECODE_METRIC, "value": round(gbs, 1), "unit": "GB/s",
+        "ms_per_step": round(ms / args.steps, 5), "scaling": scaling, "dtype": dtype, "config": cfg,
+        "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(ach / hbm, 4), "traffic": profile_traffic(f"decode_{wl}.txt"),
+                     "kernel": "decode_kernel", "kernel_ms": round(kms, 5),
+                     "algorithmic_bytes_per_launch": step_bytes},
+        "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps,
+    })
+    if not args.no_prefill and wl == "llama3_decode":
+        pre = run_prefill(dev, max(3, min(args.prefill_steps, 50)), 3, dist, peaks)
+        res["prefill"] = pre
+        res["gpu_launches"] += pre.get("steps", 0)
+    if dist.world == 1 and not args.no_cpu:
+        v, thr, desc = cpu_decode_sample(wl, args.cpu_budget)
+        res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
+                               "sample": desc}
+        if "prefill" in res and "value" in res["prefill"]:
+            pv, pthr, pdesc = cpu_prefill_sample(args.cpu_budget / 2)
+            res["prefill"]["cpu_baseline"] = {"value": round(pv, 5), "unit": "TFLOP/s", "cores": pthr,
+                                              "kind": "port", "sample": pdesc}
+    emit(res, dist)
+
+
+def e2e_decode(q, batch, ws, args, dist, step_bytes):
+    """Each step: pinned host q -> device, decode through the C ABI, result
+    -> pinned host, stream synchronised (the host holds the result)."""
+    import torch
+
+    import bml_b200
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty_like(q_host).pin_memory()
+    q_dev = torch.empty_like(q)
+    out_dev = torch.empty_like(q)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        q_dev.copy_(q_host, non_blocking=True)
+        bml_b200.decode_batched(q_dev, batch, out=out_dev, workspace=ws)
+        out_host.copy_(out_dev, non_blocking=True)
+        stream.synchronize()
+
+    n = max(10, min(args.steps, 500))
+    for _ in range(3):
+        step()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = dist.max(a.elapsed_time(b))
+    total = dist.sum(step_bytes)
+    return {"value": round(total * n / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "h2d_bytes_per_step": q_host.numel() * 4, "d2h_bytes_per_step": out_host.numel() * 4,
+            "steps": n, "ms_per_step": round(ms / n, 5)}
+
+
+def run_longctx(args, dist, peaks, res):
+    import torch
+
+    import bml_b200
+    from bml_b200 import sharding
+    dev = dist.device
+    total_len, H, Hkv, d = 131072, 32, 8, 128
+    lo, hi = sharding.kv_split_ranges(total_len, dist.world)[dist.rank]
+    gen = torch.Generator(device=dev).manual_seed(4)
+    # every rank draws the whole sequence's q; its KV slice is its own draw
+    q = gen_normal((1, H, d), torch.float32, dev, gen)
+    gen.manual_seed(4 + 1000 * (dist.rank + 1))
+    k = gen_normal((hi - lo, Hkv, d), torch.bfloat16, dev, gen)
+    v = gen_normal((hi - lo, Hkv, d), torch.bfloat16, dev, gen)
+    batch = bml_b200.SeqBatch([k], [v])
+    ws = bml_b200.Workspace(dev).ensure(1, H, d)
+    merged = torch.empty(1, H, d, dtype=torch.float32, device=dev)
+    step = sharding.KVSplitDecode(dist.pg, dist.world, H, d, dev)
+    fn = lambda: step(q, batch, ws, out=merged)  # noqa: E731
+    fn()
+    torch.cuda.synchronize()
+    ms, clocks = timed_loop(fn, args.steps, args.warmup, dist, dist.local)
+    step_bytes = decode_step_bytes(batch, H)
+    total = dist.sum(step_bytes)
+    gbs = total * args.steps / (ms * 1e-3) / 1e9
+    kfn = lambda: bml_b200.decode_partial(q, batch, workspace=ws)  # noqa: E731
+    kms = kernel_ms(kfn)
+    ach = step_bytes / (kms * 1e-3) / 1e9
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    res.update({"metric": DECODE_METRIC, "value": round(gbs, 1), "unit": "GB/s",
+                "ms_per_step": round(ms / args.steps, 5), "scaling": "strong", "dtype": "f32 (bf16 KV)",
+                "config": {"workload": "longctx", "context": total_len, "n_heads": H, "n_kv_heads": Hkv,
+                           "head_dim": d, "split": f"KV length over {dist.world} GPUs, NCCL all_gather of "
+                                                   "(m, l, o) + LSE merge",
+                           "l2": "256 MiB of KV per step on 1 GPU"},
+                "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                             "frac": round(ach / hbm, 4), "traffic": profile_traffic("decode_longctx.txt"),
+                             "kernel": "decode_kernel", "kernel_ms": round(kms, 5)},
+                "clocks": clocks, "gpu_launches": args.steps * (1 if dist.world == 1 else 2)})
+    if dist.world == 1 and not args.no_cpu:
+        v, thr, desc = cpu_decode_sample("longctx", args.cpu_budget)
+        res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
+                               "sample": desc}
+    emit(res, dist)
+
+
+def run_reference(args):
+    """CPU restatement of the reference path, timed on the host cores.  Under
+    torchrun only rank 0 works; the others exit at once."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    wl = args.workload
+    threads = oracle.num_threads()
+    total = args.steps + args.warmup
+    per_step = max(0.05, min(2.0, 60.0 / max(total, 1)))
+    if wl == "llama3_prefill":
+        unit, metric_v = "TFLOP/s", None
+        vals = []
+        for i in range(total):
+            v, thr, desc = cpu_prefill_sample(per_step)
+            if i >= args.warmup:
+                vals.append(v)
+    else:
+        unit = "GB/s"
+        vals = []
+        for i in range(total):
+            v, thr, desc = cpu_decode_sample(wl, per_step)
+            if i >= args.warmup:
+                vals.append(v)
+    metric_v = statistics.median(vals)
+    line = {"impl": "reference", "metric": DECODE_METRIC, "value": round(metric_v, 4), "unit": unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "vs_baseline": None, "dtype": "f32 dot / f64 P.V (reference arithmetic)",
+            "data": "synthetic: seeded N(0,1) (numpy PCG64)",
+            "config": {"workload": wl},
+            "cpu_baseline": {"value": round(metric_v, 4), "unit": unit, "cores": threads, "kind": "port",
+                             "sample": desc + f"; median of {len(vals)} steps"},
+            "e2e": {"value": round(metric_v, 4), "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference is Rust (no cargo/rustc here): timed via the C restatement in oracle/"}
+    print(json.dumps(line), flush=True)
+
+
+def emit(res, dist):
+    if dist.rank == 0:
+        print(json.dumps(res), flush=True)
+    dist.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--workload", default="llama3_decode",
+                    choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill"])
+    ap.add_argument("--prefill-steps", type=int, default=30)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warm-up raised to 3 steps (minimum)")
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,528 @@
+// api.cpp -- host side of the C ABI declared in include/bml_attn.h.
+//
+// Every entry point validates its arguments on the host before anything is
+// launched and reports failures through a status code and a thread-local
+// message; nothing here aborts the process.  The reference this replaces
+// (crates/compiler/src/kv_cache.rs and the attention block of
+// crates/compiler/src/gguf_compiler.rs:1008-1050 in SugarFreeDoNoSo/bml)
+// panics on out-of-range indexing; those cases return BML_E_INVALID here.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/bml_attn.h"
+#include "decode.cuh"
+#include "kv_ops.cuh"
+#include "prefill.cuh"
+
+#define BML_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+thread_local std::string g_last_error;
+
+bml_status fail(bml_status code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+bml_status ok() {
+    g_last_error.clear();
+    return BML_OK;
+}
+
+bml_status cuda_fail(cudaError_t e, const char *what) {
+    (void)cudaGetLastError();  // clear a sticky launch error of this thread
+    if (e == cudaErrorMemoryAllocation) return fail(BML_E_OOM, "%s: %s", what, cudaGetErrorString(e));
+    if (e == cudaErrorNotSupported) return fail(BML_E_UNSUPPORTED, "%s: no kernel for this shape", what);
+    return fail(BML_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CUDA_TRY(call, what)                              \
+    do {                                                  \
+        cudaError_t e_ = (call);                          \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+bool valid_dtype(int t) { return t == BML_F32 || t == BML_F16 || t == BML_BF16; }
+
+int num_sms(int device) {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    std::lock_guard<std::mutex> lk(mu);
+    if (device < 0 || device >= 64) return 148;
+    if (!cache[device]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+            n = 148;
+        cache[device] = n;
+    }
+    return cache[device];
+}
+
+int current_device() {
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess) d = 0;
+    return d;
+}
+
+// Switches to `dev` for the lifetime of the guard.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
+        else prev = -1;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+float resolve_scale(float scale, uint32_t head_dim) {
+    // gguf_compiler.rs:1010: 1/sqrt(head_dim) in f64
+    return scale < 0.f ? (float)(1.0 / sqrt((double)head_dim)) : scale;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+struct bml_kv {
+    bml_kv_desc desc;
+    std::vector<void *> k, v;  // per layer device buffers
+    uint64_t n_total_k = 0, n_total_v = 0;
+    uint32_t current_pos = 0;
+    float *staging = nullptr;  // device scratch: head_dim floats + 1
+    void *ws = nullptr;        // decode workspace for bml_attn_decode
+    size_t ws_bytes = 0;
+    size_t layer_elems() const { return (size_t)desc.max_seq_len * desc.n_kv_heads * desc.head_dim; }
+    size_t esize() const { return bml::dtype_size(desc.dtype); }
+};
+
+// ---------------------------------------------------------------------------
+// library
+// ---------------------------------------------------------------------------
+BML_API const char *bml_last_error(void) { return g_last_error.c_str(); }
+BML_API const char *bml_version(void) { return "bml-attn-b200 0.1 (sm_100a)"; }
+
+// ---------------------------------------------------------------------------
+// KV cache handle (kv_cache.rs:25-181)
+// ---------------------------------------------------------------------------
+BML_API bml_status bml_kv_create(const bml_kv_desc *desc, bml_kv **out) {
+    if (!desc || !out) return fail(BML_E_INVALID, "bml_kv_create: null argument");
+    *out = nullptr;
+    if (desc->n_layers == 0 || desc->n_kv_heads == 0 || desc->head_dim == 0 || desc->max_seq_len == 0)
+        return fail(BML_E_INVALID, "bml_kv_create: zero dimension");
+    if (!valid_dtype(desc->dtype)) return fail(BML_E_INVALID, "bml_kv_create: bad dtype %d", desc->dtype);
+    int ndev = 0;
+    CUDA_TRY(cudaGetDeviceCount(&ndev), "bml_kv_create");
+    if (desc->device < 0 || desc->device >= ndev)
+        return fail(BML_E_INVALID, "bml_kv_create: device %d of %d", desc->device, ndev);
+    DeviceGuard g(desc->device);
+    bml_kv *kv = new bml_kv();
+    kv->desc = *desc;
+    const size_t bytes = kv->layer_elems() * kv->esize();
+    kv->k.assign(desc->n_layers, nullptr);
+    kv->v.assign(desc->n_layers, nullptr);
+    cudaError_t e = cudaSuccess;
+    for (uint32_t l = 0; l < desc->n_layers && e == cudaSuccess; ++l) {
+        e = cudaMalloc(&kv->k[l], bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&kv->v[l], bytes);
+        if (e == cudaSuccess) e = cudaMemset(kv->k[l], 0, bytes);  // vec![0.0; n] (kv_cache.rs:57)
+        if (e == cudaSuccess) e = cudaMemset(kv->v[l], 0, bytes);
+    }
+    if (e == cudaSuccess) e = cudaMalloc(&kv->staging, (desc->head_dim + 4) * sizeof(float));
+    if (e != cudaSuccess) {
+        bml_kv_destroy(kv);
+        return cuda_fail(e, "bml_kv_create");
+    }
+    *out = kv;
+    return ok();
+}
+
+BML_API bml_status bml_kv_destroy(bml_kv *kv) {
+    if (!kv) return ok();
+    DeviceGuard g(kv->desc.device);
+    for (void *p : kv->k) if (p) cudaFree(p);
+    for (void *p : kv->v) if (p) cudaFree(p);
+    if (kv->staging) cudaFree(kv->staging);
+    if (kv->ws) cudaFree(kv->ws);
+    delete kv;
+    return ok();
+}
+
+static bml_status check_slot(const bml_kv *kv, int which, uint32_t layer, uint32_t pos, uint32_t kv_head,
+                             const char *fn, size_t *elem_off) {
+    if (!kv) return fail(BML_E_INVALID, "%s: null handle", fn);
+    if (which != BML_WHICH_K && which != BML_WHICH_V) return fail(BML_E_INVALID, "%s: which=%d", fn, which);
+    if (layer >= kv->desc.n_layers)
+        return fail(BML_E_INVALID, "%s: layer %u >= n_layers %u", fn, layer, kv->desc.n_layers);
+    // kv_cache.rs:83-86: ring slot; the slice start..start+d must be in range
+    const size_t stride = (size_t)kv->desc.n_kv_heads * kv->desc.head_dim;
+    const size_t start = (size_t)(pos % kv->desc.max_seq_len) * stride + (size_t)kv_head * kv->desc.head_dim;
+    if (start + kv->desc.head_dim > kv->layer_elems())
+        return fail(BML_E_INVALID, "%s: slot out of range (kv_head %u)", fn, kv_head);
+    *elem_off = start;
+    return BML_OK;
+}
+
+BML_API bml_status bml_kv_store(bml_kv *kv, int which, uint32_t layer, uint32_t pos, uint32_t kv_head,
+                                const float *host_data, size_t len) {
+    size_t off = 0;
+    bml_status st = check_slot(kv, which, layer, pos, kv_head, "bml_kv_store", &off);
+    if (st != BML_OK) return st;
+    if (!host_data) return fail(BML_E_INVALID, "bml_kv_store: null data");
+    const uint32_t d = kv->desc.head_dim;
+    // kv_cache.rs:87: copy_from_slice of data[..min(d, len)] into d slots
+    if (len < d) return fail(BML_E_INVALID, "bml_kv_store: %zu values for head_dim %u", len, d);
+    DeviceGuard g(kv->desc.device);
+    CUDA_TRY(cudaMemcpy(kv->staging, host_data, d * sizeof(float), cudaMemcpyHostToDevice), "bml_kv_store");
+    void *base = which == BML_WHICH_K ? kv->k[layer] : kv->v[layer];
+    void *dst = static_cast<char *>(base) + off * kv->esize();
+    CUDA_TRY(bml::kv_store_from_f32(kv->staging, dst, kv->desc.dtype, d, 0), "bml_kv_store");
+    CUDA_TRY(cudaStreamSynchronize(0), "bml_kv_store");
+    if (which == BML_WHICH_K) kv->n_total_k++;
+    else kv->n_total_v++;
+    return ok();
+}
+
+BML_API bml_status bml_kv_load(const bml_kv *kv, int which, uint32_t layer, uint32_t pos, uint32_t kv_head,
+                               float *host_out) {
+    size_t off = 0;
+    bml_status st = check_slot(kv, which, layer, pos, kv_head, "bml_kv_load", &off);
+    if (st != BML_OK) return st;
+    if (!host_out) return fail(BML_E_INVALID, "bml_kv_load: null output");
+    const uint32_t d = kv->desc.head_dim;
+    DeviceGuard g(kv->desc.device);
+    const void *base = which == BML_WHICH_K ? kv->k[layer] : kv->v[layer];
+    const void *src = static_cast<const char *>(base) + off * kv->esize();
+    CUDA_TRY(bml::kv_convert(src, kv->desc.dtype, kv->staging, BML_F32, d, 0), "bml_kv_load");
+    CUDA_TRY(cudaMemcpy(host_out, kv->staging, d * sizeof(float), cudaMemcpyDeviceToHost), "bml_kv_load");
+    return ok();
+}
+
+BML_API bml_status bml_kv_dot_qk(const bml_kv *kv, const float *host_q, size_t q_len, uint32_t layer,
+                                 uint32_t pos, uint32_t kv_head, float *out) {
+    size_t off = 0;
+    bml_status st = check_slot(kv, BML_WHICH_K, layer, pos, kv_head, "bml_kv_dot_qk", &off);
+    if (st != BML_OK) return st;
+    if (!out || (!host_q && q_len)) return fail(BML_E_INVALID, "bml_kv_dot_qk: null argument");
+    const uint32_t n = (uint32_t)std::min<size_t>(q_len, kv->desc.head_dim);  // zip: shorter wins
+    DeviceGuard g(kv->desc.device);
+    if (n) CUDA_TRY(cudaMemcpy(kv->staging, host_q, n * sizeof(float), cudaMemcpyHostToDevice), "bml_kv_dot_qk");
+    const void *src = static_cast<const char *>(kv->k[layer]) + off * kv->esize();
+    CUDA_TRY(bml::kv_dot(kv->staging, src, kv->desc.dtype, n, kv->staging + kv->desc.head_dim, 0),
+             "bml_kv_dot_qk");
+    CUDA_TRY(cudaMemcpy(out, kv->staging + kv->desc.head_dim, sizeof(float), cudaMemcpyDeviceToHost),
+             "bml_kv_dot_qk");
+    return ok();
+}
+
+BML_API bml_status bml_kv_stats(const bml_kv *kv, int which, uint64_t *unique, uint64_t *total, double *ratio) {
+    if (!kv || !unique || !total || !ratio) return fail(BML_E_INVALID, "bml_kv_stats: null argument");
+    if (which != BML_WHICH_K && which != BML_WHICH_V) return fail(BML_E_INVALID, "bml_kv_stats: which");
+    const uint64_t t = which == BML_WHICH_K ? kv->n_total_k : kv->n_total_v;
+    *unique = t;
+    *total = t;
+    *ratio = 1.0;
+    return ok();
+}
+
+BML_API bml_status bml_kv_byte_size(const bml_kv *kv, uint64_t *out) {
+    if (!kv || !out) return fail(BML_E_INVALID, "bml_kv_byte_size: null argument");
+    *out = (uint64_t)kv->layer_elems() * kv->esize() * kv->desc.n_layers * 2;
+    return ok();
+}
+
+BML_API bml_status bml_kv_current_pos(const bml_kv *kv, uint32_t *out) {
+    if (!kv || !out) return fail(BML_E_INVALID, "bml_kv_current_pos: null argument");
+    *out = kv->current_pos;
+    return ok();
+}
+
+BML_API bml_status bml_kv_advance(bml_kv *kv) {
+    if (!kv) return fail(BML_E_INVALID, "bml_kv_advance: null handle");
+    kv->current_pos += 1;
+    return ok();
+}
+
+BML_API bml_status bml_kv_advance_by(bml_kv *kv, uint32_t n) {
+    if (!kv) return fail(BML_E_INVALID, "bml_kv_advance_by: null handle");
+    kv->current_pos += n;
+    return ok();
+}
+
+BML_API bml_status bml_kv_layer_ptr(const bml_kv *kv, int which, uint32_t layer, void **dev_out) {
+    if (!kv || !dev_out) return fail(BML_E_INVALID, "bml_kv_layer_ptr: null argument");
+    if (which != BML_WHICH_K && which != BML_WHICH_V) return fail(BML_E_INVALID, "bml_kv_layer_ptr: which");
+    if (layer >= kv->desc.n_layers) return fail(BML_E_INVALID, "bml_kv_layer_ptr: layer %u", layer);
+    *dev_out = which == BML_WHICH_K ? kv->k[layer] : kv->v[layer];
+    return ok();
+}
+
+BML_API bml_status bml_kv_append(bml_kv *kv, uint32_t layer, uint32_t pos, const void *k_dev, const void *v_dev,
+                                 bml_dtype src_dtype, void *stream) {
+    size_t off = 0;
+    bml_status st = check_slot(kv, BML_WHICH_K, layer, pos, 0, "bml_kv_append", &off);
+    if (st != BML_OK) return st;
+    if (!k_dev || !v_dev) return fail(BML_E_INVALID, "bml_kv_append: null argument");
+    if (!valid_dtype(src_dtype)) return fail(BML_E_INVALID, "bml_kv_append: bad dtype");
+    const size_t n = (size_t)kv->desc.n_kv_heads * kv->desc.head_dim;
+    DeviceGuard g(kv->desc.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    char *kd = static_cast<char *>(kv->k[layer]) + off * kv->esize();
+    char *vd = static_cast<char *>(kv->v[layer]) + off * kv->esize();
+    CUDA_TRY(bml::kv_convert(k_dev, src_dtype, kd, kv->desc.dtype, n, s), "bml_kv_append");
+    CUDA_TRY(bml::kv_convert(v_dev, src_dtype, vd, kv->desc.dtype, n, s), "bml_kv_append");
+    kv->n_total_k += kv->desc.n_kv_heads;
+    kv->n_total_v += kv->desc.n_kv_heads;
+    return ok();
+}
+
+// ---------------------------------------------------------------------------
+// Decode
+// ---------------------------------------------------------------------------
+namespace {
+
+bml_status check_decode_shape(uint32_t n_heads, uint32_t n_kv, uint32_t head_dim, bml_dtype dt, const char *fn) {
+    if (!valid_dtype(dt)) return fail(BML_E_INVALID, "%s: bad kv dtype %d", fn, (int)dt);
+    if (n_kv == 0 || n_heads == 0 || head_dim == 0) return fail(BML_E_INVALID, "%s: zero dimension", fn);
+    // gguf_compiler.rs:1011 uses n_heads / n_kv; a remainder would make
+    // kv_h = h / group run past the last kv head, which is rejected here.
+    if (n_heads % n_kv != 0)
+        return fail(BML_E_INVALID, "%s: n_heads %u not a multiple of n_kv_heads %u", fn, n_heads, n_kv);
+    const uint32_t g = n_heads / n_kv;
+    if (!(n_kv == 1 || n_kv == 2 || n_kv == 4 || n_kv == 8))
+        return fail(BML_E_UNSUPPORTED, "%s: n_kv_heads %u (supported: 1, 2, 4, 8)", fn, n_kv);
+    if (!(g == 1 || g == 2 || g == 4 || g == 8))
+        return fail(BML_E_UNSUPPORTED, "%s: %u q heads per kv head (supported: 1, 2, 4, 8)", fn, g);
+    if (!(head_dim == 64 || head_dim == 128))
+        return fail(BML_E_UNSUPPORTED, "%s: head_dim %u (supported: 64, 128)", fn, head_dim);
+    return BML_OK;
+}
+
+// Shared body of bml_attn_decode_batched / _partial.
+bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv,
+                       uint32_t head_dim, bml_dtype dt, float scale, const float *q, float *out, float *pm,
+                       float *pl, float *po, void *workspace, size_t ws_bytes, void *stream, int mode,
+                       const char *fn) {
+    bml_status st = check_decode_shape(n_heads, n_kv, head_dim, dt, fn);
+    if (st != BML_OK) return st;
+    if (!seqs || n_seqs == 0) return fail(BML_E_INVALID, "%s: no sequences", fn);
+    if (!q || !aligned16(q)) return fail(BML_E_INVALID, "%s: q must be a 16-byte aligned device pointer", fn);
+    if (mode == bml::kModeFinal && !out) return fail(BML_E_INVALID, "%s: null output", fn);
+    if (mode == bml::kModePartial && (!pm || !pl || !po)) return fail(BML_E_INVALID, "%s: null output", fn);
+    for (uint32_t s = 0; s < n_seqs; ++s) {
+        if (seqs[s].len == 0) return fail(BML_E_INVALID, "%s: sequence %u has no positions", fn, s);
+        if (!seqs[s].k_dev || !seqs[s].v_dev || !aligned16(seqs[s].k_dev) || !aligned16(seqs[s].v_dev))
+            return fail(BML_E_INVALID, "%s: sequence %u K/V must be 16-byte aligned device pointers", fn, s);
+    }
+    const int dev = current_device();
+    const int sms = num_sms(dev);
+    bml::DecodeWorkspace ws;
+    if (!bml::decode_workspace_carve(workspace, ws_bytes, n_seqs, n_heads, head_dim, sms, &ws))
+        return fail(BML_E_INVALID, "%s: workspace of %zu bytes, need %zu", fn, ws_bytes,
+                    bml::decode_workspace_bytes(n_seqs, n_heads, head_dim, sms));
+
+    const uint32_t T = bml::decode_rows_per_tile(dt, head_dim, n_kv);
+    const float sc = resolve_scale(scale, head_dim);
+    const size_t es = bml::dtype_size(dt);
+    static thread_local bml::DecodeParams p;  // ~8 KB, kept off the stack
+    for (uint32_t base = 0; base < n_seqs; base += bml::kMaxSeqsPerLaunch) {
+        const uint32_t ns = std::min<uint32_t>(n_seqs - base, bml::kMaxSeqsPerLaunch);
+        memset(&p, 0, offsetof(bml::DecodeParams, seqs));
+        uint64_t total = 0;
+        for (uint32_t s = 0; s < ns; ++s) total += (seqs[base + s].len + T - 1) / T;
+        if (total > 0xffffffffull) return fail(BML_E_INVALID, "%s: batch too large", fn);
+        const uint32_t tpc = (uint32_t)((total + sms - 1) / sms);
+        const int grid = (int)((total + tpc - 1) / tpc);
+        uint32_t tile = 0, slot = 0;
+        for (uint32_t s = 0; s < ns; ++s) {
+            const bml_seq_desc &d = seqs[base + s];
+            const uint32_t nt = (d.len + T - 1) / T;
+            bml::DecodeSeq &e = p.seqs[s];
+            e.k = d.k_dev;
+            e.v = d.v_dev;
+            e.len = d.len;
+            e.tile_begin = tile;
+            e.slot_base = slot;
+            e.n_slots = (tile + nt - 1) / tpc - tile / tpc + 1;
+            tile += nt;
+            slot += e.n_slots;
+        }
+        if (slot > ws.max_slots) return fail(BML_E_INVALID, "%s: internal slot overflow", fn);
+        p.q = q + (size_t)base * n_heads * head_dim;
+        p.out = out ? out + (size_t)base * n_heads * head_dim : nullptr;
+        p.part_m = pm ? pm + (size_t)base * n_heads : nullptr;
+        p.part_l = pl ? pl + (size_t)base * n_heads : nullptr;
+        p.part_o = po ? po + (size_t)base * n_heads * head_dim : nullptr;
+        p.slot_ml = ws.slot_ml;
+        p.slot_o = ws.slot_o;
+        p.counters = ws.counters;
+        p.err = ws.err;
+        p.n_seqs = ns;
+        p.n_heads = n_heads;
+        p.n_kv = n_kv;
+        p.rows_per_tile = T;
+        p.total_tiles = (uint32_t)total;
+        p.tiles_per_cta = tpc;
+        p.row_bytes = (uint32_t)(n_kv * head_dim * es);
+        p.qscale = (float)((double)sc * 1.4426950408889634);
+        p.mode = mode;
+        CUDA_TRY(bml::launch_decode(p, dt, head_dim, n_heads / n_kv, grid, static_cast<cudaStream_t>(stream)), fn);
+    }
+    return ok();
+}
+
+}  // namespace
+
+BML_API bml_status bml_attn_decode_workspace_size(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
+                                                  int32_t device, size_t *bytes) {
+    if (!bytes) return fail(BML_E_INVALID, "bml_attn_decode_workspace_size: null output");
+    if (n_seqs == 0 || n_heads == 0 || head_dim == 0)
+        return fail(BML_E_INVALID, "bml_attn_decode_workspace_size: zero dimension");
+    *bytes = bml::decode_workspace_bytes(n_seqs, n_heads, head_dim, num_sms(device));
+    return ok();
+}
+
+BML_API bml_status bml_attn_decode_batched(const bml_seq_desc *seqs_host, uint32_t n_seqs, uint32_t n_heads,
+                                           uint32_t n_kv_heads, uint32_t head_dim, bml_dtype kv_dtype, float scale,
+                                           const float *q_dev, float *out_dev, void *workspace,
+                                           size_t workspace_bytes, void *stream) {
+    return decode_impl(seqs_host, n_seqs, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev, nullptr,
+                       nullptr, nullptr, workspace, workspace_bytes, stream, bml::kModeFinal,
+                       "bml_attn_decode_batched");
+}
+
+BML_API bml_status bml_attn_decode_partial(const bml_seq_desc *seqs_host, uint32_t n_seqs, uint32_t n_heads,
+                                           uint32_t n_kv_heads, uint32_t head_dim, bml_dtype kv_dtype, float scale,
+                                           const float *q_dev, float *m_dev, float *l_dev, float *o_dev,
+                                           void *workspace, size_t workspace_bytes, void *stream) {
+    return decode_impl(seqs_host, n_seqs, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, nullptr, m_dev,
+                       l_dev, o_dev, workspace, workspace_bytes, stream, bml::kModePartial,
+                       "bml_attn_decode_partial");
+}
+
+BML_API bml_status bml_attn_decode(bml_kv *kv, uint32_t layer, uint32_t pos, uint32_t n_heads, float scale,
+                                   const float *q_dev, float *out_dev, void *stream) {
+    if (!kv) return fail(BML_E_INVALID, "bml_attn_decode: null handle");
+    if (layer >= kv->desc.n_layers) return fail(BML_E_INVALID, "bml_attn_decode: layer %u", layer);
+    if (pos >= kv->desc.max_seq_len)
+        return fail(BML_E_INVALID, "bml_attn_decode: pos %u >= max_seq_len %u (ring wrap not reproduced)", pos,
+                    kv->desc.max_seq_len);
+    bml_status st = check_decode_shape(n_heads, kv->desc.n_kv_heads, kv->desc.head_dim, kv->desc.dtype,
+                                       "bml_attn_decode");
+    if (st != BML_OK) return st;
+    DeviceGuard g(kv->desc.device);
+    const size_t need = bml::decode_workspace_bytes(1, n_heads, kv->desc.head_dim, num_sms(kv->desc.device));
+    if (kv->ws_bytes < need) {
+        if (kv->ws) cudaFree(kv->ws);
+        kv->ws = nullptr;
+        kv->ws_bytes = 0;
+        CUDA_TRY(cudaMalloc(&kv->ws, need), "bml_attn_decode");
+        CUDA_TRY(cudaMemset(kv->ws, 0, need), "bml_attn_decode");
+        kv->ws_bytes = need;
+    }
+    bml_seq_desc d{kv->k[layer], kv->v[layer], pos + 1, 0};
+    return decode_impl(&d, 1, n_heads, kv->desc.n_kv_heads, kv->desc.head_dim, kv->desc.dtype, scale, q_dev,
+                       out_dev, nullptr, nullptr, nullptr, kv->ws, kv->ws_bytes, stream, bml::kModeFinal,
+                       "bml_attn_decode");
+}
+
+BML_API bml_status bml_attn_merge_lse(const float *m_dev, const float *l_dev, const float *o_dev, uint32_t n_parts,
+                                      uint32_t n_rows, uint32_t head_dim, float *out_dev, void *stream) {
+    if (!m_dev || !l_dev || !o_dev || !out_dev) return fail(BML_E_INVALID, "bml_attn_merge_lse: null argument");
+    if (n_parts == 0 || head_dim == 0) return fail(BML_E_INVALID, "bml_attn_merge_lse: zero dimension");
+    CUDA_TRY(bml::launch_merge_lse(m_dev, l_dev, o_dev, n_parts, n_rows, head_dim, out_dev,
+                                   static_cast<cudaStream_t>(stream)),
+             "bml_attn_merge_lse");
+    return ok();
+}
+
+BML_API bml_status bml_attn_merge_lse_packed(const float *parts_dev, uint32_t n_parts, uint32_t n_rows,
+                                             uint32_t head_dim, float *out_dev, void *stream) {
+    if (!parts_dev || !out_dev) return fail(BML_E_INVALID, "bml_attn_merge_lse_packed: null argument");
+    if (n_parts == 0 || head_dim == 0) return fail(BML_E_INVALID, "bml_attn_merge_lse_packed: zero dimension");
+    CUDA_TRY(bml::launch_merge_lse_packed(parts_dev, n_parts, n_rows, head_dim, out_dev,
+                                          static_cast<cudaStream_t>(stream)),
+             "bml_attn_merge_lse_packed");
+    return ok();
+}
+
+BML_API bml_status bml_attn_workspace_check(void *workspace, size_t workspace_bytes, void *stream) {
+    if (!workspace || workspace_bytes < 256) return fail(BML_E_INVALID, "bml_attn_workspace_check: workspace");
+    uint32_t err = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    CUDA_TRY(cudaMemcpyAsync(&err, workspace, sizeof err, cudaMemcpyDeviceToHost, s), "bml_attn_workspace_check");
+    CUDA_TRY(cudaStreamSynchronize(s), "bml_attn_workspace_check");
+    if (err) {
+        const uint32_t zero = 0;
+        CUDA_TRY(cudaMemcpyAsync(workspace, &zero, sizeof zero, cudaMemcpyHostToDevice, s),
+                 "bml_attn_workspace_check");
+        CUDA_TRY(cudaStreamSynchronize(s), "bml_attn_workspace_check");
+        return fail(BML_E_TIMEOUT, "a bounded device wait gave up (error word 0x%x)", err);
+    }
+    return ok();
+}
+
+// ---------------------------------------------------------------------------
+// Prefill
+// ---------------------------------------------------------------------------
+BML_API bml_status bml_attn_prefill(const void *q_dev, const void *k_dev, const void *v_dev, uint32_t n_seqs,
+                                    uint32_t seq_len, uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                                    bml_dtype in_dtype, float scale, int causal, void *out_dev,
+                                    bml_dtype out_dtype, void *stream) {
+    const char *fn = "bml_attn_prefill";
+    if (!q_dev || !k_dev || !v_dev || !out_dev) return fail(BML_E_INVALID, "%s: null argument", fn);
+    if (!aligned16(q_dev) || !aligned16(k_dev) || !aligned16(v_dev) || !aligned16(out_dev))
+        return fail(BML_E_INVALID, "%s: pointers must be 16-byte aligned", fn);
+    if (n_seqs == 0 || seq_len == 0 || n_heads == 0 || n_kv_heads == 0)
+        return fail(BML_E_INVALID, "%s: zero dimension", fn);
+    if (n_heads % n_kv_heads != 0)
+        return fail(BML_E_INVALID, "%s: n_heads %u not a multiple of n_kv_heads %u", fn, n_heads, n_kv_heads);
+    if (!(in_dtype == BML_BF16 || in_dtype == BML_F16))
+        return fail(BML_E_UNSUPPORTED, "%s: inputs must be bf16 or f16", fn);
+    if (!(out_dtype == BML_F32 || out_dtype == in_dtype))
+        return fail(BML_E_INVALID, "%s: out dtype must be f32 or the input dtype", fn);
+    if (!(head_dim == 64 || head_dim == 128))
+        return fail(BML_E_UNSUPPORTED, "%s: head_dim %u (supported: 64, 128)", fn, head_dim);
+    bml::PrefillArgs a;
+    a.q = q_dev;
+    a.k = k_dev;
+    a.v = v_dev;
+    a.out = out_dev;
+    a.n_seqs = n_seqs;
+    a.seq_len = seq_len;
+    a.n_heads = n_heads;
+    a.n_kv = n_kv_heads;
+    a.head_dim = head_dim;
+    a.in_dtype = in_dtype;
+    a.out_dtype = out_dtype;
+    a.scale = resolve_scale(scale, head_dim);
+    a.causal = causal != 0;
+    a.num_sms = num_sms(current_device());
+    CUDA_TRY(bml::launch_prefill(a, static_cast<cudaStream_t>(stream)), fn);
+    return ok();
+}
+
+// ---------------------------------------------------------------------------
+// softmax_f32 (kv_cache.rs:188-200)
+// ---------------------------------------------------------------------------
+BML_API bml_status bml_softmax_f32(const float *x_dev, uint32_t n_rows, uint32_t n, float *out_dev, void *stream) {
+    if (n == 0 || n_rows == 0) return ok();  // empty in, empty out (kv_cache.rs:189-191)
+    if (!x_dev || !out_dev) return fail(BML_E_INVALID, "bml_softmax_f32: null argument");
+    CUDA_TRY(bml::softmax_rows(x_dev, n_rows, n, out_dev, static_cast<cudaStream_t>(stream)), "bml_softmax_f32");
+    return ok();
+}

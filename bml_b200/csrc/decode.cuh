@@ -1,0 +1,72 @@
+// decode.cuh -- launch interface of the split-K flash-decoding kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace bml {
+
+// Per-sequence entry of a decode launch (host-computed schedule).
+struct DecodeSeq {
+    const void *k;        // [len][n_kv][D]
+    const void *v;
+    uint32_t len;         // positions attended
+    uint32_t tile_begin;  // first global tile of this sequence
+    uint32_t slot_base;   // first partial slot of this sequence
+    uint32_t n_slots;     // CTAs that touch this sequence
+};
+
+constexpr int kMaxSeqsPerLaunch = 256;
+
+enum DecodeMode : int { kModeFinal = 0, kModePartial = 1 };
+
+struct DecodeParams {
+    const float *q;        // [n_seqs][n_heads][D] f32
+    float *out;            // final outputs [n_seqs][n_heads][D]
+    float *part_m;         // partial-mode outputs [n_seqs][n_heads]
+    float *part_l;
+    float *part_o;         // [n_seqs][n_heads][D]
+    float *slot_ml;        // scratch [n_slots][n_heads][2]
+    float *slot_o;         // scratch [n_slots][n_heads][D]
+    uint32_t *counters;    // scratch [n_seqs], zero between calls
+    uint32_t *err;         // scratch error word
+    uint32_t n_seqs, n_heads, n_kv;
+    uint32_t rows_per_tile;   // T
+    uint32_t total_tiles;
+    uint32_t tiles_per_cta;
+    uint32_t row_bytes;       // n_kv * D * sizeof(elem)
+    float qscale;             // scale * log2(e)
+    int mode;
+    DecodeSeq seqs[kMaxSeqsPerLaunch];
+};
+
+// Scratch layout inside a caller workspace.
+struct DecodeWorkspace {
+    uint32_t *err;
+    uint32_t *counters;
+    float *slot_ml;
+    float *slot_o;
+    size_t max_slots;
+};
+
+size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
+                              int num_sms);
+bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads,
+                            uint32_t head_dim, int num_sms, DecodeWorkspace *out);
+
+// Rows of one tile for a (dtype, head_dim, n_kv) combination.
+uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv);
+
+// Launches one decode kernel; returns a CUDA error code.  The kernel is
+// selected from (dtype, head_dim, group); unsupported combinations return
+// cudaErrorNotSupported.
+cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim,
+                          uint32_t group, int grid, cudaStream_t stream);
+
+cudaError_t launch_merge_lse(const float *m, const float *l, const float *o, uint32_t n_parts,
+                             uint32_t n_rows, uint32_t head_dim, float *out,
+                             cudaStream_t stream);
+
+cudaError_t launch_merge_lse_packed(const float *parts, uint32_t n_parts, uint32_t n_rows,
+                                    uint32_t head_dim, float *out, cudaStream_t stream);
+
+}  // namespace bml

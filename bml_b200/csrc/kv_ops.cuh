@@ -1,0 +1,16 @@
+// kv_ops.cuh -- launch interface of the KV-cache and softmax kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace bml {
+
+cudaError_t kv_store_from_f32(const float *src_dev, void *dst_dev, bml_dtype dst_t, size_t n,
+                              cudaStream_t st);
+cudaError_t kv_convert(const void *src_dev, bml_dtype src_t, void *dst_dev, bml_dtype dst_t, size_t n,
+                       cudaStream_t st);
+cudaError_t kv_dot(const float *q_dev, const void *k_dev, bml_dtype t, uint32_t n, float *out_dev,
+                   cudaStream_t st);
+cudaError_t softmax_rows(const float *x_dev, uint32_t n_rows, uint32_t n, float *out_dev, cudaStream_t st);
+
+}  // namespace bml
