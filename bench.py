@@ -313,13 +313,13 @@ def cpu_prefill_sample(budget_s: float):
 # ---------------------------------------------------------------------------
 # arms
 # ---------------------------------------------------------------------------
-def run_prefill(dev, steps, warmup, dist, peaks):
+def run_prefill(dev, steps, warmup, dist, peaks, n=4, S=8192):
     import torch
 
     import bml_b200
     from bml_b200 import workloads as W
     gen = torch.Generator(device=dev).manual_seed(3 + 1000 * dist.rank)
-    n, S, H, Hkv, d = 4, 8192, 32, 8, 128
+    H, Hkv, d = 32, 8, 128
     q = gen_normal((n, S, H, d), torch.bfloat16, dev, gen)
     k = gen_normal((n, S, Hkv, d), torch.bfloat16, dev, gen)
     v = gen_normal((n, S, Hkv, d), torch.bfloat16, dev, gen)
@@ -359,7 +359,7 @@ def run_b200(args):
            "peak_source": f"{peak_kind} ({PEAKS_PATH if peak_kind == 'measured' else 'fallback'})"}
     wl = args.workload
     if wl == "llama3_prefill":
-        pre = run_prefill(dev, args.steps, args.warmup, dist, peaks)
+        pre = run_prefill(dev, args.steps, args.warmup, dist, peaks, args.prefill_n, args.prefill_s)
         res.update(pre)
         res.update({"metric": DECODE_METRIC, "dtype": "bf16", "scaling": "weak", "gpu_launches": args.steps})
         emit(res, dist)
@@ -560,6 +560,8 @@ def main():
     ap.add_argument("--workload", default="llama3_decode",
                     choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill"])
     ap.add_argument("--prefill-steps", type=int, default=30)
+    ap.add_argument("--prefill-n", type=int, default=4, help="prefill sequences (llama3_prefill)")
+    ap.add_argument("--prefill-s", type=int, default=8192, help="prefill tokens per sequence")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)

@@ -42,7 +42,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
            "-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared",
            "-o", LIB + ".tmp", *sources()]
     if verbose:
-        cmd.insert(4, "-Xptxas=-v")
+        cmd.insert(3, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
     os.replace(LIB + ".tmp", LIB)

@@ -136,6 +136,11 @@ struct Elem<float> {
         out[2] = __uint_as_float(c.z);
         out[3] = __uint_as_float(c.w);
     }
+    // element pairs (2i, 2i+1) as float2, for the packed f32x2 FMA
+    __device__ __forceinline__ static void widen2(const uint4 &c, float2 *out) {
+        out[0] = make_float2(__uint_as_float(c.x), __uint_as_float(c.y));
+        out[1] = make_float2(__uint_as_float(c.z), __uint_as_float(c.w));
+    }
 };
 
 template <>
@@ -149,6 +154,11 @@ struct Elem<__nv_bfloat16> {
             out[2 * i] = __uint_as_float(w[i] << 16);
             out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
         }
+    }
+    __device__ __forceinline__ static void widen2(const uint4 &c, float2 *out) {
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) out[i] = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
     }
 };
 
@@ -165,6 +175,11 @@ struct Elem<__half> {
             out[2 * i] = f.x;
             out[2 * i + 1] = f.y;
         }
+    }
+    __device__ __forceinline__ static void widen2(const uint4 &c, float2 *out) {
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) out[i] = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
     }
 };
 

@@ -12,9 +12,10 @@
 //    flattened list of (sequence, tile) work, so ragged batches balance to
 //    within one tile per SM.  A tile is T consecutive positions of ALL kv
 //    heads, which is one contiguous run of T*n_kv*D elements.
-//  * A producer warp streams tiles into a 4-stage shared-memory ring with
-//    1-D TMA bulk copies (cp.async.bulk, L2 evict-first) completing on
-//    mbarriers; consumers release stages through a second mbarrier ring.
+//  * Thread 0 streams tiles into a 4-stage shared-memory ring with 1-D TMA
+//    bulk copies (cp.async.bulk, L2 evict-first) completing on mbarriers;
+//    the 8 warps release stages through a second mbarrier ring and thread 0
+//    refills a stage once all of them have released it.
 //  * 8 consumer warps: warp w serves kv head w % n_kv.  Inside a warp, 8
 //    lanes share one KV row (16-byte conflict-free shared loads), so a warp
 //    covers 4 rows per step.  q for the G heads of the group stays in
@@ -38,27 +39,31 @@ namespace {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads + 32;
-constexpr int kStageKBytes = 16384;  // K bytes per stage; V the same
-constexpr int kStages = 4;
+constexpr int kThreads = kConsumerThreads;
+constexpr int kSmemBudget = 227 * 1024;
 
-template <typename KT, int D>
-struct Geo {
+template <typename KT, int D, int G>
+struct Cfg {
     static constexpr int ES = sizeof(KT);
     static constexpr int HEAD_BYTES = D * ES;
     static constexpr int CHUNKS = HEAD_BYTES / 16;
     static constexpr int CPL = CHUNKS / 8;  // 16-byte chunks per lane
     static constexpr int EPC = 16 / ES;     // elements per chunk
     static constexpr int E = CPL * EPC;     // elements per lane
-    // rows per warp per step = 4; stage bytes = STEPS * 4 * 8 warps * HEAD_BYTES
-    static constexpr int STEPS = kStageKBytes / (32 * HEAD_BYTES);
+    static constexpr int E2 = E / 2;        // float2 pairs per lane
+    static constexpr int STAGE_K = 32768;   // K bytes per stage; V the same
+    // rows per warp per step = 4; stage bytes = STEPS * 4 rows * 8 warps * HEAD_BYTES
+    static constexpr int STEPS = STAGE_K / (32 * HEAD_BYTES);
+    static constexpr int WSCR = 4 * G /*alpha*/ + 4 * STEPS * G /*p*/ + 4 * G * 2 /*ml*/;
+    static constexpr int EXTRA = 2 * 8 * 8 /*barriers*/ + 16 +
+                                 4 * (kConsumerWarps * WSCR + kConsumerWarps * G * D + kConsumerWarps * G * 2);
+    static constexpr int STAGES_FIT = (kSmemBudget - EXTRA) / (2 * STAGE_K);
+    static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
+    static constexpr int BAR_OFF = STAGES * 2 * STAGE_K;
+    static constexpr int SMEM = BAR_OFF + EXTRA;
     static_assert(CHUNKS % 8 == 0, "head row must be a multiple of 128 bytes");
     static_assert(STEPS >= 1, "stage too small");
-};
-
-template <int G>
-struct Smem {
-    static constexpr int kWscr = 4 * G /*alpha*/ + 4 * 4 * G /*p, STEPS<=4*/ + 4 * G * 2 /*ml*/;
+    static_assert(STAGES >= 2, "shared memory budget");
 };
 
 __device__ __forceinline__ uint32_t seq_of_tile(const DecodeParams &p, uint32_t t) {
@@ -101,20 +106,19 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[G], int j) {
 }
 
 template <typename KT, int D, int G>
-__global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodeParams p) {
-    using Gm = Geo<KT, D>;
-    constexpr int STEPS = Gm::STEPS, E = Gm::E, CPL = Gm::CPL, EPC = Gm::EPC;
-    constexpr int HEAD_BYTES = Gm::HEAD_BYTES;
-    constexpr int WSCR = Smem<G>::kWscr;
-    static_assert(STEPS <= 4, "scratch sized for at most 4 steps");
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+    using C = Cfg<KT, D, G>;
+    constexpr int STEPS = C::STEPS, E2 = C::E2, CPL = C::CPL, EPC = C::EPC;
+    constexpr int HEAD_BYTES = C::HEAD_BYTES, STAGE_K = C::STAGE_K, NST = C::STAGES;
+    constexpr int WSCR = C::WSCR;
     constexpr float NEG_INF = -INFINITY;
 
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *stages = smem;
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kStages * 2 * kStageKBytes);
-    uint64_t *empty = full + kStages;
-    volatile uint32_t *flags = reinterpret_cast<volatile uint32_t *>(empty + kStages);
-    float *wscr = reinterpret_cast<float *>(smem + kStages * 2 * kStageKBytes + 2 * kStages * 8 + 16);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+    uint64_t *empty = full + 8;
+    volatile uint32_t *flags = reinterpret_cast<volatile uint32_t *>(empty + 8);
+    float *wscr = reinterpret_cast<float *>(smem + C::BAR_OFF + 2 * 8 * 8 + 16);
     float *wsum = wscr + kConsumerWarps * WSCR;  // [8 warps][G][D]
     float *wml = wsum + kConsumerWarps * G * D;  // [8 warps][G][2]
 
@@ -124,7 +128,7 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
     const uint32_t T = p.rows_per_tile;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kStages; ++i) {
+        for (int i = 0; i < NST; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], kConsumerWarps);
         }
@@ -135,31 +139,34 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
     __syncthreads();
     if (t_begin >= t_end) return;
 
-    // ------------------------------------------------------------ producer
-    if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            const uint64_t pol = l2_policy_evict_first();
-            uint32_t s = seq_of_tile(p, t_begin);
-            for (uint32_t t = t_begin, it = 0; t < t_end; ++t, ++it) {
-                while (t >= tile_end_of(p, s)) ++s;
-                const uint32_t stage = it % kStages;
-                if (it >= kStages)
-                    mbar_wait(&empty[stage], ((it / kStages) & 1u) ^ 1u, flags, p.err);
-                const uint32_t row0 = (t - p.seqs[s].tile_begin) * T;
-                const uint32_t rows = min(T, p.seqs[s].len - row0);
-                const uint32_t bytes = rows * p.row_bytes;
-                uint8_t *sk = stages + stage * 2 * kStageKBytes;
-                mbar_arrive_expect_tx(&full[stage], 2 * bytes);
-                const uint8_t *gk = static_cast<const uint8_t *>(p.seqs[s].k) + (size_t)row0 * p.row_bytes;
-                const uint8_t *gv = static_cast<const uint8_t *>(p.seqs[s].v) + (size_t)row0 * p.row_bytes;
-                bulk_g2s_stream(sk, gk, bytes, &full[stage], pol);
-                bulk_g2s_stream(sk + kStageKBytes, gv, bytes, &full[stage], pol);
-            }
-        }
-        return;
+    // Thread 0 doubles as the producer: it fills the ring ahead of the
+    // consumers and refills a stage as soon as all 8 warps released it.
+    // (A separate producer warp would make 9 warps; the register file is
+    // split over 4 sub-partitions, and a 3-warp partition caps a thread at
+    // 168 registers, below what the consumers need.)
+    uint64_t pol = 0;
+    uint32_t ps = 0, pt = t_begin;  // producer cursor: sequence, tile
+    auto issue = [&](uint32_t it) {
+        while (pt >= tile_end_of(p, ps)) ++ps;
+        const uint32_t stage = it % NST;
+        const uint32_t row0 = (pt - p.seqs[ps].tile_begin) * T;
+        const uint32_t rows = min(T, p.seqs[ps].len - row0);
+        const uint32_t bytes = rows * p.row_bytes;
+        uint8_t *sk = stages + stage * 2 * STAGE_K;
+        mbar_arrive_expect_tx(&full[stage], 2 * bytes);
+        const uint8_t *gk = static_cast<const uint8_t *>(p.seqs[ps].k) + (size_t)row0 * p.row_bytes;
+        const uint8_t *gv = static_cast<const uint8_t *>(p.seqs[ps].v) + (size_t)row0 * p.row_bytes;
+        bulk_g2s_stream(sk, gk, bytes, &full[stage], pol);
+        bulk_g2s_stream(sk + STAGE_K, gv, bytes, &full[stage], pol);
+        ++pt;
+    };
+    const uint32_t n_tiles = t_end - t_begin;
+    if (threadIdx.x == 0) {
+        pol = l2_policy_evict_first();
+        ps = seq_of_tile(p, t_begin);
+        for (uint32_t it = 0; it < n_tiles && it < (uint32_t)NST; ++it) issue(it);
     }
 
-    // ------------------------------------------------------------ consumers
     const int n_kv = (int)p.n_kv;
     const int nwh = kConsumerWarps / n_kv;  // warps per kv head
     const int h = warp % n_kv, ph = warp / n_kv;
@@ -169,9 +176,9 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
     float *scr = wscr + warp * WSCR;
     float *s_alpha = scr;               // [4][G]
     float *s_p = scr + 4 * G;           // [4][STEPS][G]
-    float *s_ml = s_p + 4 * 4 * G;      // [4][G][2]
+    float *s_ml = s_p + 4 * STEPS * G;  // [4][G][2]
 
-    float q[G][E], acc[G][E];
+    float2 q2[G][E2], acc[G][E2];
     float m_own = NEG_INF, l_own = 0.f;
 
     uint32_t s = seq_of_tile(p, t_begin);
@@ -185,52 +192,53 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
 #pragma unroll
                 for (int f = 0; f < EPC / 4; ++f) {
                     const float4 v = __ldg(src + f);
-                    q[hh][c * EPC + 4 * f + 0] = v.x * p.qscale;
-                    q[hh][c * EPC + 4 * f + 1] = v.y * p.qscale;
-                    q[hh][c * EPC + 4 * f + 2] = v.z * p.qscale;
-                    q[hh][c * EPC + 4 * f + 3] = v.w * p.qscale;
+                    q2[hh][(c * EPC) / 2 + 2 * f + 0] = make_float2(v.x * p.qscale, v.y * p.qscale);
+                    q2[hh][(c * EPC) / 2 + 2 * f + 1] = make_float2(v.z * p.qscale, v.w * p.qscale);
                 }
             }
         }
 #pragma unroll
         for (int hh = 0; hh < G; ++hh)
 #pragma unroll
-            for (int e = 0; e < E; ++e) acc[hh][e] = 0.f;
+            for (int e = 0; e < E2; ++e) acc[hh][e] = make_float2(0.f, 0.f);
         m_own = NEG_INF;
         l_own = 0.f;
     };
     load_q(s);
 
     for (uint32_t t = t_begin, it = 0; t < t_end; ++t, ++it) {
-        const uint32_t stage = it % kStages;
-        mbar_wait(&full[stage], (it / kStages) & 1u, flags, p.err);
+        const uint32_t stage = it % NST;
+        mbar_wait(&full[stage], (it / NST) & 1u, flags, p.err);
         const uint32_t row0 = (t - p.seqs[s].tile_begin) * T;
         const uint32_t rows = min(T, p.seqs[s].len - row0);
-        const uint8_t *sk = stages + stage * 2 * kStageKBytes + h * HEAD_BYTES;
-        const uint8_t *sv = sk + kStageKBytes;
+        const uint8_t *sk = stages + stage * 2 * STAGE_K + h * HEAD_BYTES;
+        const uint8_t *sv = sk + STAGE_K;
 
         // pass 1: scores of this lane group's rows (log2 domain)
         float sc[STEPS];
 #pragma unroll
         for (int st = 0; st < STEPS; ++st) {
             const uint32_t r = (uint32_t)((st * nwh + ph) * 4 + grp);
-            float part[G];
+            float2 part2[G];
 #pragma unroll
-            for (int hh = 0; hh < G; ++hh) part[hh] = 0.f;
+            for (int hh = 0; hh < G; ++hh) part2[hh] = make_float2(0.f, 0.f);
             if (r < rows) {
                 const uint8_t *rowp = sk + (size_t)r * p.row_bytes;
 #pragma unroll
                 for (int c = 0; c < CPL; ++c) {
                     const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (j + 8 * c) * 16);
-                    float kf[EPC];
-                    Elem<KT>::widen(raw, kf);
+                    float2 kf[EPC / 2];
+                    Elem<KT>::widen2(raw, kf);
 #pragma unroll
                     for (int hh = 0; hh < G; ++hh)
 #pragma unroll
-                        for (int e = 0; e < EPC; ++e)
-                            part[hh] = fmaf(q[hh][c * EPC + e], kf[e], part[hh]);
+                        for (int e = 0; e < EPC / 2; ++e)
+                            part2[hh] = __ffma2_rn(q2[hh][c * (EPC / 2) + e], kf[e], part2[hh]);
                 }
             }
+            float part[G];
+#pragma unroll
+            for (int hh = 0; hh < G; ++hh) part[hh] = part2[hh].x + part2[hh].y;
             const float tot = transpose_reduce<G>(part, j);
             sc[st] = (r < rows) ? tot : NEG_INF;
         }
@@ -265,9 +273,11 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
         }
         if (__any_sync(0xffffffffu, moved)) {
 #pragma unroll
-            for (int hh = 0; hh < G; ++hh)
+            for (int hh = 0; hh < G; ++hh) {
+                const float2 a2 = make_float2(al[hh], al[hh]);
 #pragma unroll
-                for (int e = 0; e < E; ++e) acc[hh][e] *= al[hh];
+                for (int e = 0; e < E2; ++e) acc[hh][e] = __fmul2_rn(acc[hh][e], a2);
+            }
         }
 
         // pass 2: P.V
@@ -275,25 +285,32 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
         for (int st = 0; st < STEPS; ++st) {
             const uint32_t r = (uint32_t)((st * nwh + ph) * 4 + grp);
             if (r < rows) {
-                float pp[G];
+                float2 pp[G];
 #pragma unroll
-                for (int hh = 0; hh < G; ++hh) pp[hh] = s_p[(grp * STEPS + st) * G + hh];
+                for (int hh = 0; hh < G; ++hh) {
+                    const float pv = s_p[(grp * STEPS + st) * G + hh];
+                    pp[hh] = make_float2(pv, pv);
+                }
                 const uint8_t *rowp = sv + (size_t)r * p.row_bytes;
 #pragma unroll
                 for (int c = 0; c < CPL; ++c) {
                     const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (j + 8 * c) * 16);
-                    float vf[EPC];
-                    Elem<KT>::widen(raw, vf);
+                    float2 vf[EPC / 2];
+                    Elem<KT>::widen2(raw, vf);
 #pragma unroll
                     for (int hh = 0; hh < G; ++hh)
 #pragma unroll
-                        for (int e = 0; e < EPC; ++e)
-                            acc[hh][c * EPC + e] = fmaf(pp[hh], vf[e], acc[hh][c * EPC + e]);
+                        for (int e = 0; e < EPC / 2; ++e)
+                            acc[hh][c * (EPC / 2) + e] = __ffma2_rn(pp[hh], vf[e], acc[hh][c * (EPC / 2) + e]);
                 }
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
+        if (threadIdx.x == 0 && it + NST < n_tiles) {
+            mbar_wait(&empty[stage], (it / NST) & 1u, flags, p.err);
+            issue(it + NST);
+        }
 
         const bool last_of_cta = (t + 1 == t_end);
         const bool seq_done = (t + 1 == tile_end_of(p, s));
@@ -324,15 +341,18 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
             }
             Mh[hh] = M;
             Lh[hh] = L;
+            const float2 f2 = make_float2(mine, mine);
 #pragma unroll
-            for (int e = 0; e < E; ++e) acc[hh][e] *= mine;
+            for (int e = 0; e < E2; ++e) acc[hh][e] = __fmul2_rn(acc[hh][e], f2);
         }
 #pragma unroll
         for (int hh = 0; hh < G; ++hh)
 #pragma unroll
-            for (int e = 0; e < E; ++e) {
-                acc[hh][e] += __shfl_xor_sync(0xffffffffu, acc[hh][e], 8);
-                acc[hh][e] += __shfl_xor_sync(0xffffffffu, acc[hh][e], 16);
+            for (int e = 0; e < E2; ++e) {
+                acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 8);
+                acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 8);
+                acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 16);
+                acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 16);
             }
         float *ws = wsum + warp * G * D;
         if (grp == 0) {
@@ -341,7 +361,8 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
 #pragma unroll
                 for (int c = 0; c < CPL; ++c)
 #pragma unroll
-                    for (int e = 0; e < EPC; ++e) ws[hh * D + (j + 8 * c) * EPC + e] = acc[hh][c * EPC + e];
+                    for (int e = 0; e < EPC / 2; ++e)
+                        *reinterpret_cast<float2 *>(ws + hh * D + (j + 8 * c) * EPC + 2 * e) = acc[hh][c * (EPC / 2) + e];
         }
         if (lane == 0) {
 #pragma unroll
@@ -437,21 +458,16 @@ __global__ void __maxnreg__(224) decode_kernel(const __grid_constant__ DecodePar
 }
 
 template <typename KT, int D, int G>
-size_t smem_bytes() {
-    return (size_t)kStages * 2 * kStageKBytes + 2 * kStages * 8 + 16 +
-           sizeof(float) * ((size_t)kConsumerWarps * Smem<G>::kWscr + (size_t)kConsumerWarps * G * D +
-                            (size_t)kConsumerWarps * G * 2);
-}
-
-template <typename KT, int D, int G>
 cudaError_t launch_one(const DecodeParams &p, int grid, cudaStream_t stream) {
-    const size_t smem = smem_bytes<KT, D, G>();
-    static bool configured = false;  // per process: attribute is per function
-    if (!configured) {
+    constexpr int smem = Cfg<KT, D, G>::SMEM;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
         cudaError_t e = cudaFuncSetAttribute(decode_kernel<KT, D, G>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        configured = true;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
     }
     decode_kernel<KT, D, G><<<grid, kThreads, smem, stream>>>(p);
     return cudaGetLastError();
@@ -521,9 +537,9 @@ __global__ void merge_lse_packed_kernel(const float *__restrict__ parts, uint32_
 }  // namespace
 
 uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv) {
-    const uint32_t head_bytes = head_dim * (uint32_t)dtype_size(dt);
-    const uint32_t steps = kStageKBytes / (32 * head_bytes);
-    return steps * 4 * (kConsumerWarps / n_kv);
+    // STEPS * 4 rows * (8 / n_kv) warps per head; equal to STAGE_K / row_bytes
+    const uint32_t row_bytes = n_kv * head_dim * (uint32_t)dtype_size(dt);
+    return 32768u / row_bytes;
 }
 
 size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, int num_sms) {

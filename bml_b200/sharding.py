@@ -76,7 +76,7 @@ class KVSplitDecode:
         size = packed_size(n_rows, self.d)
         if self._packed is None or self._packed.numel() != size:
             self._packed = torch.empty(size, dtype=torch.float32, device=self.device)
-            self._gathered = torch.empty(self.world, size, dtype=torch.float32, device=self.device)
+            self._gathered = torch.empty(self.world * size, dtype=torch.float32, device=self.device)
         return self._packed, self._gathered
 
     def __call__(self, q, batch, workspace=None, out=None):
@@ -94,7 +94,7 @@ class KVSplitDecode:
             self.partial_fn(q, batch, m, l_, o)
         if self.world > 1:
             self.pg.all_gather_into_tensor(gathered, packed)
-            parts = gathered
+            parts = gathered.view(self.world, -1)
         else:
             parts = packed.view(1, -1)
         if out is None:
