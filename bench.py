@@ -75,12 +75,13 @@ def profile_traffic(name: str):
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, torch_index: int):
         self.proc = None
+        self.t0 = self.t1 = None
         try:
             import torch
             p = torch.cuda.get_device_properties(torch_index)
@@ -91,7 +92,14 @@ class ClockSampler:
         except Exception as e:  # no nvidia-smi: report no clocks
             log("clock sampler unavailable:", e)
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def stop(self):
+        import datetime
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         self.proc.terminate()
@@ -104,8 +112,16 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                continue
+            # keep only samples taken inside the timed region
+            if self.t0 is not None and not (self.t0 - 0.05 <= ts <= (self.t1 or ts) + 0.05):
+                continue
+            f = f[1:]
             try:
                 sm.append(float(f[1]))
                 smax.append(float(f[2]))
@@ -183,11 +199,13 @@ def timed_loop(fn, steps: int, warmup: int, dist: Dist, sampler_index: int):
     sampler = ClockSampler(sampler_index)
     time.sleep(0.25)  # let the sampler start before the timed region
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.mark_start()
     start.record(stream)
     for _ in range(steps):
         fn()
     end.record(stream)
     torch.cuda.synchronize()
+    sampler.mark_end()
     clocks = sampler.stop()
     dist.barrier()
     ms = start.elapsed_time(end)
@@ -410,7 +428,7 @@ def run_b200(args):
         "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps,
     })
     if not args.no_prefill and wl == "llama3_decode":
-        pre = run_prefill(dev, max(3, min(args.prefill_steps, 50)), 3, dist, peaks)
+        pre = run_prefill(dev, max(3, args.prefill_steps), 3, dist, peaks)
         res["prefill"] = pre
         res["gpu_launches"] += pre.get("steps", 0)
     if dist.world == 1 and not args.no_cpu:
@@ -559,7 +577,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="llama3_decode",
                     choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill"])
-    ap.add_argument("--prefill-steps", type=int, default=30)
+    ap.add_argument("--prefill-steps", type=int, default=200)
     ap.add_argument("--prefill-n", type=int, default=4, help="prefill sequences (llama3_prefill)")
     ap.add_argument("--prefill-s", type=int, default=8192, help="prefill tokens per sequence")
     ap.add_argument("--no-prefill", action="store_true")
