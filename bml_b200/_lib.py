@@ -67,6 +67,8 @@ SIGNATURES = {
     "bml_attn_decode_workspace_size": (_st, [_u32, _u32, _u32, _i32, C.POINTER(_sz)]),
     "bml_attn_decode_batched": (_st, [C.POINTER(bml_seq_desc), _u32, _u32, _u32, _u32, C.c_int,
                                       C.c_float, _vp, _vp, _vp, _sz, _vp]),
+    "bml_attn_decode_batched_noalloc": (_st, [C.POINTER(bml_seq_desc), _u32, _u32, _u32, _u32, C.c_int,
+                                              C.c_float, _vp, _vp, _vp]),
     "bml_attn_decode_partial": (_st, [C.POINTER(bml_seq_desc), _u32, _u32, _u32, _u32, C.c_int,
                                       C.c_float, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "bml_attn_merge_lse": (_st, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp]),

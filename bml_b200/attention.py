@@ -169,6 +169,29 @@ def decode_batched(q: torch.Tensor, ks, vs=None, scale: float = -1.0, out: torch
     return out
 
 
+def decode_batched_noalloc(q: torch.Tensor, ks, vs=None, scale: float = -1.0,
+                           out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """decode_batched without a workspace, for callers that cannot allocate
+    device memory (a pool allocator that owns all of it, or a serving loop
+    that must not pay cudaMalloc's device-wide synchronisation).  Scratch is
+    the library's fixed 4 MiB device array: larger batches raise
+    BmlInvalid, and calls that overlap in time on the GPU race (serialise
+    them).  The first call on a device should come before any stream
+    capture."""
+    b = _as_batch(ks, vs)
+    _need(q, "q", torch.float32, 3)
+    n_seqs, n_heads, d = q.shape
+    if n_seqs != len(b) or d != b.head_dim:
+        raise ValueError("q does not match the batch")
+    if out is None:
+        out = torch.empty_like(q)
+    else:
+        _need(out, "out", torch.float32)
+    L.call("bml_attn_decode_batched_noalloc", b.descs, n_seqs, n_heads, b.n_kv, d, dtype_code(b.dtype),
+           float(scale), _ptr(q), _ptr(out), _stream(stream))
+    return out
+
+
 def decode_partial(q: torch.Tensor, ks, vs=None, scale: float = -1.0,
                    workspace: Workspace | None = None, stream=None,
                    m: torch.Tensor | None = None, l: torch.Tensor | None = None,

@@ -526,3 +526,68 @@ BML_API bml_status bml_softmax_f32(const float *x_dev, uint32_t n_rows, uint32_t
     CUDA_TRY(bml::softmax_rows(x_dev, n_rows, n, out_dev, static_cast<cudaStream_t>(stream)), "bml_softmax_f32");
     return ok();
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free batched decode.
+//
+// Some callers cannot call cudaMalloc at all: a host runtime that hands all
+// device memory to its own pool allocator when it starts, or a serving loop
+// in which cudaMalloc's implicit device-wide synchronisation would stall
+// the other streams.  For them this entry point takes its split-K scratch
+// from a fixed array in device global memory instead of a caller workspace.
+// ---------------------------------------------------------------------------
+namespace {
+
+// 4 MiB: on a 148-SM B200, enough for 64 sequences x 32 heads x d=128 (the
+// 32-sequence Llama-3 decode batch needs 3.0 MB).
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+
+// Every GPU that loads this library holds this array until the process
+// exits.  In host code its name is only a stand-in: the device address comes
+// from cudaGetSymbolAddress.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the scratch array on the current device; looked up once
+// per device, with that device current.
+bml_status noalloc_scratch(int dev, void **out) {
+    if (dev < 0 || dev >= 64) return fail(BML_E_INVALID, "bml_attn_decode_batched_noalloc: device %d", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) return cuda_fail(e, "bml_attn_decode_batched_noalloc: cudaGetSymbolAddress");
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return BML_OK;
+}
+
+}  // namespace
+
+BML_API bml_status bml_attn_decode_batched_noalloc(const bml_seq_desc *seqs_host, uint32_t n_seqs,
+                                                   uint32_t n_heads, uint32_t n_kv_heads, uint32_t head_dim,
+                                                   bml_dtype kv_dtype, float scale, const float *q_dev,
+                                                   float *out_dev, void *stream) {
+    const char *fn = "bml_attn_decode_batched_noalloc";
+    bml_status st = check_decode_shape(n_heads, n_kv_heads, head_dim, kv_dtype, fn);
+    if (st != BML_OK) return st;
+    if (!seqs_host || n_seqs == 0) return fail(BML_E_INVALID, "%s: no sequences", fn);
+    const int dev = current_device();
+    const size_t need = bml::decode_workspace_bytes(n_seqs, n_heads, head_dim, num_sms(dev));
+    if (need > kNoAllocScratchBytes)
+        return fail(BML_E_INVALID, "%s: needs %zu bytes of scratch, above the fixed %zu-byte maximum", fn, need,
+                    kNoAllocScratchBytes);
+    void *scratch = nullptr;
+    st = noalloc_scratch(dev, &scratch);
+    if (st != BML_OK) return st;
+    // Every call shares the array, which keeps the last call's contents:
+    // clear the error word and the merge tickets, which must start at zero.
+    const size_t seqs = n_seqs < (uint32_t)bml::kMaxSeqsPerLaunch ? n_seqs : bml::kMaxSeqsPerLaunch;
+    const size_t zero_bytes = 256 + ((seqs * 4 + 255) / 256) * 256;
+    CUDA_TRY(cudaMemsetAsync(scratch, 0, zero_bytes, static_cast<cudaStream_t>(stream)), fn);
+    return decode_impl(seqs_host, n_seqs, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev, nullptr,
+                       nullptr, nullptr, scratch, kNoAllocScratchBytes, stream, bml::kModeFinal, fn);
+}

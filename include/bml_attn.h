@@ -182,6 +182,30 @@ bml_status bml_attn_decode_batched(const bml_seq_desc *seqs_host,
                                    void *workspace, size_t workspace_bytes,
                                    void *stream);
 
+/* Allocation-free variant of bml_attn_decode_batched.  It has no
+ * counterpart in the reference.  It is for callers that cannot call
+ * cudaMalloc: a host runtime that hands all device memory to its own pool
+ * allocator at start-up, or a serving loop in which cudaMalloc's implicit
+ * device-wide synchronisation would stall other streams.  It takes no
+ * workspace; its scratch is a fixed 4 MiB array in device global memory
+ * that every GPU loading this library holds until the process exits, and it
+ * allocates nothing itself.  A call that would need more scratch than that
+ * (bml_attn_decode_workspace_size for the same arguments above 4 MiB, e.g.
+ * 256 sequences of 64 heads at head_dim 128) returns BML_E_INVALID.  The
+ * first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the one array, which keeps the last call's contents: each
+ * call first clears the merge tickets and error word on `stream`, so calls
+ * that overlap in time on the GPU race with each other and must be
+ * serialised (one stream, or events between streams).  Results equal
+ * bml_attn_decode_batched's.  Asynchronous. */
+bml_status bml_attn_decode_batched_noalloc(const bml_seq_desc *seqs_host,
+                                           uint32_t n_seqs, uint32_t n_heads,
+                                           uint32_t n_kv_heads, uint32_t head_dim,
+                                           bml_dtype kv_dtype, float scale,
+                                           const float *q_dev, float *out_dev,
+                                           void *stream);
+
 /* KV-split partial: the same computation over each sequence's slice of the
  * cache, returning per (sequence, q head) the running max m (in log2
  * units: max over positions of scale*log2(e)*q.k), the softmax
