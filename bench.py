@@ -66,9 +66,18 @@ def profile_traffic(name: str):
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
                 return float(line.split(":", 1)[1].split()[0])
-    except OSError:
+    except (OSError, ValueError, IndexError):
         pass
     return None
+
+
+def host_threads() -> int:
+    """Every host core this process may run on (torchrun sets
+    OMP_NUM_THREADS=1, which must not throttle the CPU baseline)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 # ---------------------------------------------------------------------------
@@ -277,7 +286,7 @@ def cpu_decode_sample(workload: str, budget_s: float):
 
     import oracle
     from bml_b200 import workloads as W
-    threads = oracle.num_threads()
+    threads = host_threads()
     if workload == "batched_tinyllama":
         q, ks, vs = W.batched_tinyllama(n_seqs=8)
         code, nkv, d, es = None, 4, 64, 2
@@ -311,7 +320,7 @@ def cpu_prefill_sample(budget_s: float):
     prefill; returns TFLOP/s (causal pairs actually computed)."""
     import oracle
     from bml_b200 import workloads as W
-    threads = oracle.num_threads()
+    threads = host_threads()
     S = 8192
     q, k, v = W.llama3_prefill(n_seqs=1, seq_len=S)
     rows = (S - 16, S)
@@ -530,9 +539,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import oracle
     wl = args.workload
-    threads = oracle.num_threads()
+    threads = host_threads()
     total = args.steps + args.warmup
     per_step = max(0.05, min(2.0, 60.0 / max(total, 1)))
     if wl == "llama3_prefill":

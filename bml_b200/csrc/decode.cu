@@ -37,13 +37,14 @@ namespace bml {
 
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kThreads = kConsumerThreads;
 constexpr int kSmemBudget = 227 * 1024;
 
-template <typename KT, int D, int G>
+// Kernel geometry.  NW warps; warp w serves kv head w % n_kv, the w-th
+// "head split" (GW of the G q heads sharing that kv head) and a row phase.
+template <typename KT, int D, int G, int GW, int NW>
 struct Cfg {
+    static constexpr int THREADS = NW * 32;
+    static constexpr int HS = G / GW;       // head splits per kv head
     static constexpr int ES = sizeof(KT);
     static constexpr int HEAD_BYTES = D * ES;
     static constexpr int CHUNKS = HEAD_BYTES / 16;
@@ -52,15 +53,17 @@ struct Cfg {
     static constexpr int E = CPL * EPC;     // elements per lane
     static constexpr int E2 = E / 2;        // float2 pairs per lane
     static constexpr int STAGE_K = 32768;   // K bytes per stage; V the same
-    // rows per warp per step = 4; stage bytes = STEPS * 4 rows * 8 warps * HEAD_BYTES
-    static constexpr int STEPS = STAGE_K / (32 * HEAD_BYTES);
-    static constexpr int WSCR = 4 * G /*alpha*/ + 4 * STEPS * G /*p*/ + 4 * G * 2 /*ml*/;
+    // rows per tile T = STAGE_K / (n_kv*HEAD_BYTES); rows per warp = T / nph
+    // with nph = NW / (n_kv*HS); 4 rows per warp step.
+    static constexpr int STEPS = STAGE_K * HS / (HEAD_BYTES * NW * 4);
+    static constexpr int WSCR = 4 * GW /*alpha*/ + 4 * STEPS * GW /*p*/ + 4 * GW * 2 /*ml*/;
     static constexpr int EXTRA = 2 * 8 * 8 /*barriers*/ + 16 +
-                                 4 * (kConsumerWarps * WSCR + kConsumerWarps * G * D + kConsumerWarps * G * 2);
+                                 4 * (NW * WSCR + NW * GW * D + NW * GW * 2);
     static constexpr int STAGES_FIT = (kSmemBudget - EXTRA) / (2 * STAGE_K);
     static constexpr int STAGES = STAGES_FIT > 4 ? 4 : STAGES_FIT;
     static constexpr int BAR_OFF = STAGES * 2 * STAGE_K;
     static constexpr int SMEM = BAR_OFF + EXTRA;
+    static_assert(G % GW == 0, "head split");
     static_assert(CHUNKS % 8 == 0, "head row must be a multiple of 128 bytes");
     static_assert(STEPS >= 1, "stage too small");
     static_assert(STAGES >= 2, "shared memory budget");
@@ -105,12 +108,12 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[G], int j) {
     return v[0];
 }
 
-template <typename KT, int D, int G>
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
-    using C = Cfg<KT, D, G>;
-    constexpr int STEPS = C::STEPS, E2 = C::E2, CPL = C::CPL, EPC = C::EPC;
+template <typename KT, int D, int G, int GW, int NW>
+__global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+    using C = Cfg<KT, D, G, GW, NW>;
+    constexpr int STEPS = C::STEPS, E2 = C::E2, CPL = C::CPL, EPC = C::EPC, HS = C::HS;
     constexpr int HEAD_BYTES = C::HEAD_BYTES, STAGE_K = C::STAGE_K, NST = C::STAGES;
-    constexpr int WSCR = C::WSCR;
+    constexpr int WSCR = C::WSCR, THREADS = C::THREADS;
     constexpr float NEG_INF = -INFINITY;
 
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -119,8 +122,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     uint64_t *empty = full + 8;
     volatile uint32_t *flags = reinterpret_cast<volatile uint32_t *>(empty + 8);
     float *wscr = reinterpret_cast<float *>(smem + C::BAR_OFF + 2 * 8 * 8 + 16);
-    float *wsum = wscr + kConsumerWarps * WSCR;  // [8 warps][G][D]
-    float *wml = wsum + kConsumerWarps * G * D;  // [8 warps][G][2]
+    float *wsum = wscr + NW * WSCR;  // [NW warps][GW][D]
+    float *wml = wsum + NW * GW * D;  // [NW warps][GW][2]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t t_begin = blockIdx.x * p.tiles_per_cta;
@@ -130,7 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     if (threadIdx.x == 0) {
         for (int i = 0; i < NST; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kConsumerWarps);
+            mbar_init(&empty[i], NW);
         }
         flags[0] = 0u;
         flags[1] = 0u;
@@ -140,10 +143,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     if (t_begin >= t_end) return;
 
     // Thread 0 doubles as the producer: it fills the ring ahead of the
-    // consumers and refills a stage as soon as all 8 warps released it.
-    // (A separate producer warp would make 9 warps; the register file is
-    // split over 4 sub-partitions, and a 3-warp partition caps a thread at
-    // 168 registers, below what the consumers need.)
+    // consumers and refills a stage as soon as every warp released it.
+    // (A separate producer warp would unbalance the 4 sub-partitions of the
+    // SM, whose register files each serve a quarter of the warps.)
     uint64_t pol = 0;
     uint32_t ps = 0, pt = t_begin;  // producer cursor: sequence, tile
     auto issue = [&](uint32_t it) {
@@ -168,24 +170,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
 
     const int n_kv = (int)p.n_kv;
-    const int nwh = kConsumerWarps / n_kv;  // warps per kv head
-    const int h = warp % n_kv, ph = warp / n_kv;
+    const int nph = NW / (n_kv * HS);  // row phases per (kv head, head split)
+    const int h = warp % n_kv;
+    const int hs = (warp / n_kv) % HS;
+    const int ph = warp / (n_kv * HS);
     const int grp = lane >> 3, j = lane & 7;
-    const int own = (j * G) >> 3;
-    const bool owner_lane = (j & ((8 / G) - 1)) == 0;
+    const int own = (j * GW) >> 3;
+    const bool owner_lane = (j & ((8 / GW) - 1)) == 0;
     float *scr = wscr + warp * WSCR;
-    float *s_alpha = scr;               // [4][G]
-    float *s_p = scr + 4 * G;           // [4][STEPS][G]
-    float *s_ml = s_p + 4 * STEPS * G;  // [4][G][2]
+    float *s_alpha = scr;                // [4][GW]
+    float *s_p = scr + 4 * GW;           // [4][STEPS][GW]
+    float *s_ml = s_p + 4 * STEPS * GW;  // [4][GW][2]
 
-    float2 q2[G][E2], acc[G][E2];
+    float2 q2[GW][E2], acc[GW][E2];
     float m_own = NEG_INF, l_own = 0.f;
 
     uint32_t s = seq_of_tile(p, t_begin);
     auto load_q = [&](uint32_t seq) {
-        const float *qs = p.q + ((size_t)seq * p.n_heads + (size_t)h * G) * D;
+        const float *qs = p.q + ((size_t)seq * p.n_heads + (size_t)h * G + (size_t)hs * GW) * D;
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
+        for (int hh = 0; hh < GW; ++hh) {
 #pragma unroll
             for (int c = 0; c < CPL; ++c) {
                 const float4 *src = reinterpret_cast<const float4 *>(qs + hh * D + (j + 8 * c) * EPC);
@@ -198,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             }
         }
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh)
+        for (int hh = 0; hh < GW; ++hh)
 #pragma unroll
             for (int e = 0; e < E2; ++e) acc[hh][e] = make_float2(0.f, 0.f);
         m_own = NEG_INF;
@@ -209,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     for (uint32_t t = t_begin, it = 0; t < t_end; ++t, ++it) {
         const uint32_t stage = it % NST;
         mbar_wait(&full[stage], (it / NST) & 1u, flags, p.err);
+        __syncwarp();  // lanes leave the spin separately; the shuffles below need the whole warp
         const uint32_t row0 = (t - p.seqs[s].tile_begin) * T;
         const uint32_t rows = min(T, p.seqs[s].len - row0);
         const uint8_t *sk = stages + stage * 2 * STAGE_K + h * HEAD_BYTES;
@@ -218,10 +223,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         float sc[STEPS];
 #pragma unroll
         for (int st = 0; st < STEPS; ++st) {
-            const uint32_t r = (uint32_t)((st * nwh + ph) * 4 + grp);
-            float2 part2[G];
+            const uint32_t r = (uint32_t)((st * nph + ph) * 4 + grp);
+            float2 part2[GW];
 #pragma unroll
-            for (int hh = 0; hh < G; ++hh) part2[hh] = make_float2(0.f, 0.f);
+            for (int hh = 0; hh < GW; ++hh) part2[hh] = make_float2(0.f, 0.f);
             if (r < rows) {
                 const uint8_t *rowp = sk + (size_t)r * p.row_bytes;
 #pragma unroll
@@ -230,16 +235,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                     float2 kf[EPC / 2];
                     Elem<KT>::widen2(raw, kf);
 #pragma unroll
-                    for (int hh = 0; hh < G; ++hh)
+                    for (int hh = 0; hh < GW; ++hh)
 #pragma unroll
                         for (int e = 0; e < EPC / 2; ++e)
                             part2[hh] = __ffma2_rn(q2[hh][c * (EPC / 2) + e], kf[e], part2[hh]);
                 }
             }
-            float part[G];
+            float part[GW];
 #pragma unroll
-            for (int hh = 0; hh < G; ++hh) part[hh] = part2[hh].x + part2[hh].y;
-            const float tot = transpose_reduce<G>(part, j);
+            for (int hh = 0; hh < GW; ++hh) part[hh] = part2[hh].x + part2[hh].y;
+            const float tot = transpose_reduce<GW>(part, j);
             sc[st] = (r < rows) ? tot : NEG_INF;
         }
         float mt = sc[0];
@@ -257,23 +262,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         l_own = l_own * alpha + psum;
         m_own = m_new;
         if (owner_lane) {
-            s_alpha[grp * G + own] = alpha;
+            s_alpha[grp * GW + own] = alpha;
 #pragma unroll
-            for (int st = 0; st < STEPS; ++st) s_p[(grp * STEPS + st) * G + own] = sc[st];
+            for (int st = 0; st < STEPS; ++st) s_p[(grp * STEPS + st) * GW + own] = sc[st];
         }
         __syncwarp();
 
         // rescale the accumulators when a running max moved
-        float al[G];
+        float al[GW];
         bool moved = false;
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
-            al[hh] = s_alpha[grp * G + hh];
+        for (int hh = 0; hh < GW; ++hh) {
+            al[hh] = s_alpha[grp * GW + hh];
             moved |= (al[hh] != 1.f);
         }
         if (__any_sync(0xffffffffu, moved)) {
 #pragma unroll
-            for (int hh = 0; hh < G; ++hh) {
+            for (int hh = 0; hh < GW; ++hh) {
                 const float2 a2 = make_float2(al[hh], al[hh]);
 #pragma unroll
                 for (int e = 0; e < E2; ++e) acc[hh][e] = __fmul2_rn(acc[hh][e], a2);
@@ -283,12 +288,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         // pass 2: P.V
 #pragma unroll
         for (int st = 0; st < STEPS; ++st) {
-            const uint32_t r = (uint32_t)((st * nwh + ph) * 4 + grp);
+            const uint32_t r = (uint32_t)((st * nph + ph) * 4 + grp);
             if (r < rows) {
-                float2 pp[G];
+                float2 pp[GW];
 #pragma unroll
-                for (int hh = 0; hh < G; ++hh) {
-                    const float pv = s_p[(grp * STEPS + st) * G + hh];
+                for (int hh = 0; hh < GW; ++hh) {
+                    const float pv = s_p[(grp * STEPS + st) * GW + hh];
                     pp[hh] = make_float2(pv, pv);
                 }
                 const uint8_t *rowp = sv + (size_t)r * p.row_bytes;
@@ -298,7 +303,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                     float2 vf[EPC / 2];
                     Elem<KT>::widen2(raw, vf);
 #pragma unroll
-                    for (int hh = 0; hh < G; ++hh)
+                    for (int hh = 0; hh < GW; ++hh)
 #pragma unroll
                         for (int e = 0; e < EPC / 2; ++e)
                             acc[hh][c * (EPC / 2) + e] = __ffma2_rn(pp[hh], vf[e], acc[hh][c * (EPC / 2) + e]);
@@ -318,18 +323,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 
         // ---------------------------------------------- finalize sequence s
         if (owner_lane) {
-            s_ml[(grp * G + own) * 2 + 0] = m_own;
-            s_ml[(grp * G + own) * 2 + 1] = l_own;
+            s_ml[(grp * GW + own) * 2 + 0] = m_own;
+            s_ml[(grp * GW + own) * 2 + 1] = l_own;
         }
         __syncwarp();
-        float Mh[G], Lh[G];
+        float Mh[GW], Lh[GW];
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh) {
+        for (int hh = 0; hh < GW; ++hh) {
             float mg[4], lg[4];
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
-                mg[g] = s_ml[(g * G + hh) * 2 + 0];
-                lg[g] = s_ml[(g * G + hh) * 2 + 1];
+                mg[g] = s_ml[(g * GW + hh) * 2 + 0];
+                lg[g] = s_ml[(g * GW + hh) * 2 + 1];
             }
             const float M = fmaxf(fmaxf(mg[0], mg[1]), fmaxf(mg[2], mg[3]));
             float L = 0.f, mine = 0.f;
@@ -346,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             for (int e = 0; e < E2; ++e) acc[hh][e] = __fmul2_rn(acc[hh][e], f2);
         }
 #pragma unroll
-        for (int hh = 0; hh < G; ++hh)
+        for (int hh = 0; hh < GW; ++hh)
 #pragma unroll
             for (int e = 0; e < E2; ++e) {
                 acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 8);
@@ -354,10 +359,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 16);
                 acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 16);
             }
-        float *ws = wsum + warp * G * D;
+        float *ws = wsum + warp * GW * D;
         if (grp == 0) {
 #pragma unroll
-            for (int hh = 0; hh < G; ++hh)
+            for (int hh = 0; hh < GW; ++hh)
 #pragma unroll
                 for (int c = 0; c < CPL; ++c)
 #pragma unroll
@@ -366,30 +371,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         }
         if (lane == 0) {
 #pragma unroll
-            for (int hh = 0; hh < G; ++hh) {
-                wml[(warp * G + hh) * 2 + 0] = Mh[hh];
-                wml[(warp * G + hh) * 2 + 1] = Lh[hh];
+            for (int hh = 0; hh < GW; ++hh) {
+                wml[(warp * GW + hh) * 2 + 0] = Mh[hh];
+                wml[(warp * GW + hh) * 2 + 1] = Lh[hh];
             }
         }
-        named_bar_sync(1, kConsumerThreads);
+        named_bar_sync(1, THREADS);
 
         const DecodeSeq &sq = p.seqs[s];
         const bool single = (sq.n_slots == 1);
         const uint32_t slot = sq.slot_base + (blockIdx.x - sq.tile_begin / p.tiles_per_cta);
         const uint32_t total = p.n_heads * D;
         const int tid = threadIdx.x;
-        for (uint32_t idx = tid; idx < total; idx += kConsumerThreads) {
+        for (uint32_t idx = tid; idx < total; idx += THREADS) {
             const uint32_t qh = idx / D, d = idx % D;
-            const uint32_t hk = qh / G, hh = qh % G;
+            const uint32_t hk = qh / G, hsplit = (qh % G) / GW, hh = qh % GW;
+            const int wbase = (int)hk + n_kv * (int)hsplit;  // warp of row phase 0
             float M = NEG_INF;
-            for (int w = 0; w < nwh; ++w) M = fmaxf(M, wml[((hk + w * n_kv) * G + hh) * 2]);
+            for (int w = 0; w < nph; ++w) M = fmaxf(M, wml[((wbase + w * n_kv * HS) * GW + hh) * 2]);
             float L = 0.f, O = 0.f;
-            for (int w = 0; w < nwh; ++w) {
-                const int ww = hk + w * n_kv;
-                const float mw = wml[(ww * G + hh) * 2];
+            for (int w = 0; w < nph; ++w) {
+                const int ww = wbase + w * n_kv * HS;
+                const float mw = wml[(ww * GW + hh) * 2];
                 const float f = (mw == NEG_INF) ? 0.f : fast_exp2(mw - M);
-                L += wml[(ww * G + hh) * 2 + 1] * f;
-                O += wsum[(ww * G + hh) * D + d] * f;
+                L += wml[(ww * GW + hh) * 2 + 1] * f;
+                O += wsum[(ww * GW + hh) * D + d] * f;
             }
             const float o = O / L;
             const size_t row = (size_t)s * p.n_heads + qh;
@@ -411,17 +417,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 }
             }
         }
-        if (!single) {
+        if (!single && p.merge_in_kernel) {
             __threadfence();
-            named_bar_sync(1, kConsumerThreads);
+            named_bar_sync(1, THREADS);
             if (tid == 0) {
                 const uint32_t old = atomicAdd(&p.counters[s], 1u);
                 flags[1] = (old == sq.n_slots - 1) ? 1u : 0u;
             }
-            named_bar_sync(1, kConsumerThreads);
+            named_bar_sync(1, THREADS);
             if (flags[1]) {
                 __threadfence();
-                for (uint32_t idx = tid; idx < total; idx += kConsumerThreads) {
+                for (uint32_t idx = tid; idx < total; idx += THREADS) {
                     const uint32_t qh = idx / D, d = idx % D;
                     float M = NEG_INF;
                     for (uint32_t i = 0; i < sq.n_slots; ++i)
@@ -449,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 if (tid == 0) p.counters[s] = 0u;
             }
         }
-        named_bar_sync(1, kConsumerThreads);
+        named_bar_sync(1, THREADS);
         if (!last_of_cta) {
             ++s;
             load_q(s);
@@ -457,29 +463,42 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
 }
 
-template <typename KT, int D, int G>
+template <typename KT, int D, int G, int GW, int NW>
 cudaError_t launch_one(const DecodeParams &p, int grid, cudaStream_t stream) {
-    constexpr int smem = Cfg<KT, D, G>::SMEM;
+    using C = Cfg<KT, D, G, GW, NW>;
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KT, D, G>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KT, D, G, GW, NW>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    decode_kernel<KT, D, G><<<grid, kThreads, smem, stream>>>(p);
+    decode_kernel<KT, D, G, GW, NW><<<grid, C::THREADS, C::SMEM, stream>>>(p);
     return cudaGetLastError();
+}
+
+// Warp layout per (dtype, head_dim, group): GW q heads per warp so that q and
+// the accumulators fit in the register budget of 16 warps (<= 128 registers
+// a thread); shapes whose kv heads times head splits exceed 16 warps use 8
+// warps with all G heads in a warp.
+template <typename KT, int D, int G>
+cudaError_t launch_shape(const DecodeParams &p, int grid, cudaStream_t stream) {
+    constexpr int E2 = (D * (int)sizeof(KT) / 128) * (16 / (int)sizeof(KT)) / 2;
+    constexpr int GW = G <= 1 ? 1 : (G * E2 <= 16 ? G : (16 / E2 >= 1 ? 16 / E2 : 1));
+    constexpr int HS = G / GW;
+    if ((int)p.n_kv * HS <= 16) return launch_one<KT, D, G, GW, 16>(p, grid, stream);
+    return launch_one<KT, D, G, G, 8>(p, grid, stream);
 }
 
 template <typename KT, int D>
 cudaError_t launch_g(const DecodeParams &p, uint32_t group, int grid, cudaStream_t stream) {
     switch (group) {
-        case 1: return launch_one<KT, D, 1>(p, grid, stream);
-        case 2: return launch_one<KT, D, 2>(p, grid, stream);
-        case 4: return launch_one<KT, D, 4>(p, grid, stream);
-        case 8: return launch_one<KT, D, 8>(p, grid, stream);
+        case 1: return launch_shape<KT, D, 1>(p, grid, stream);
+        case 2: return launch_shape<KT, D, 2>(p, grid, stream);
+        case 4: return launch_shape<KT, D, 4>(p, grid, stream);
+        case 8: return launch_shape<KT, D, 8>(p, grid, stream);
         default: return cudaErrorNotSupported;
     }
 }
@@ -534,7 +553,67 @@ __global__ void merge_lse_packed_kernel(const float *__restrict__ parts, uint32_
     out[idx] = O / L;
 }
 
+// One CTA per (sequence, head) row of a sequence with several slots: the
+// slot weights 2^(m_i - M) l_i are computed once per slot in shared memory,
+// then each thread accumulates one output element over the slots in order.
+__global__ void __launch_bounds__(128) slot_merge_kernel(const __grid_constant__ DecodeParams p,
+                                                         uint32_t head_dim) {
+    __shared__ float w[1024];
+    __shared__ float red[4];
+    const uint32_t s = blockIdx.x / p.n_heads, qh = blockIdx.x % p.n_heads;
+    const DecodeSeq &sq = p.seqs[s];
+    if (sq.n_slots <= 1) return;  // written directly by the decode kernel
+    const uint32_t n = min(sq.n_slots, 1024u);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float mx = -INFINITY;
+    for (uint32_t i = tid; i < n; i += blockDim.x)
+        mx = fmaxf(mx, __ldcg(&p.slot_ml[((size_t)(sq.slot_base + i) * p.n_heads + qh) * 2]));
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float lsum = 0.f;
+    for (uint32_t i = tid; i < n; i += blockDim.x) {
+        const size_t sr = (size_t)(sq.slot_base + i) * p.n_heads + qh;
+        const float mi = __ldcg(&p.slot_ml[sr * 2]);
+        const float f = (mi == -INFINITY) ? 0.f : fast_exp2(mi - M) * __ldcg(&p.slot_ml[sr * 2 + 1]);
+        w[i] = f;
+        lsum += f;
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, m);
+    if (lane == 0) red[warp] = lsum;
+    __syncthreads();
+    const float L = (red[0] + red[1]) + (red[2] + red[3]);
+    const size_t row = (size_t)s * p.n_heads + qh;
+    for (uint32_t d = tid; d < head_dim; d += blockDim.x) {
+        float O = 0.f;
+        const float *src = p.slot_o + ((size_t)sq.slot_base * p.n_heads + qh) * head_dim + d;
+        const size_t stride = (size_t)p.n_heads * head_dim;
+#pragma unroll 8
+        for (uint32_t i = 0; i < n; ++i) O += __ldcg(src + i * stride) * w[i];
+        if (p.mode == kModeFinal) {
+            p.out[row * head_dim + d] = O / L;
+        } else {
+            p.part_o[row * head_dim + d] = O / L;
+            if (d == 0) {
+                p.part_m[row] = M;
+                p.part_l[row] = L;
+            }
+        }
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_slot_merge(const DecodeParams &p, uint32_t head_dim, cudaStream_t stream) {
+    const unsigned blocks = p.n_seqs * p.n_heads;
+    if (blocks == 0) return cudaSuccess;
+    slot_merge_kernel<<<blocks, 128, 0, stream>>>(p, head_dim);
+    return cudaGetLastError();
+}
 
 uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv) {
     // STEPS * 4 rows * (8 / n_kv) warps per head; equal to STAGE_K / row_bytes
@@ -542,26 +621,37 @@ uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv) {
     return 32768u / row_bytes;
 }
 
+// Scratch layout, fixed part first so that calls of any shape agree on it:
+//   [0, 256)                  error word
+//   [256, 256 + kTicketBytes) merge tickets: one per (sequence, kv head) of a
+//                             launch (256 sequences x 8 kv heads at most); each
+//                             call leaves them zero
+//   then partial slots for (2*seqs + SMs) split points of n_heads rows each.
+// A shape-dependent ticket area would let one call read another call's
+// leftover slot values as tickets.
+constexpr size_t kTicketBytes = (size_t)kMaxSeqsPerLaunch * 8 * 4;
+
 size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, int num_sms) {
     const size_t seqs = n_seqs < (uint32_t)kMaxSeqsPerLaunch ? n_seqs : kMaxSeqsPerLaunch;
-    const size_t slots = seqs + (size_t)num_sms;
-    size_t b = 256;                                     // error word
-    b += ((seqs * 4 + 255) / 256) * 256;                // counters
-    b += ((slots * n_heads * 2 * 4 + 255) / 256) * 256; // slot (m, l)
-    b += slots * n_heads * head_dim * 4;                // slot o
+    const size_t slots = 2 * seqs + (size_t)num_sms;
+    size_t b = 256 + kTicketBytes;
+    b += ((slots * n_heads * 2 * 4 + 255) / 256) * 256;   // slot (m, l)
+    b += slots * n_heads * head_dim * 4;                  // slot o
     return b;
 }
 
-bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads,
-                            uint32_t head_dim, int num_sms, DecodeWorkspace *out) {
+size_t decode_workspace_zero_bytes() { return 256 + kTicketBytes; }
+
+bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
+                            int num_sms, DecodeWorkspace *out) {
     if (!ws || bytes < decode_workspace_bytes(n_seqs, n_heads, head_dim, num_sms)) return false;
     const size_t seqs = n_seqs < (uint32_t)kMaxSeqsPerLaunch ? n_seqs : kMaxSeqsPerLaunch;
-    const size_t slots = seqs + (size_t)num_sms;
+    const size_t slots = 2 * seqs + (size_t)num_sms;
     uint8_t *b = static_cast<uint8_t *>(ws);
     out->err = reinterpret_cast<uint32_t *>(b);
     b += 256;
     out->counters = reinterpret_cast<uint32_t *>(b);
-    b += ((seqs * 4 + 255) / 256) * 256;
+    b += kTicketBytes;
     out->slot_ml = reinterpret_cast<float *>(b);
     b += ((slots * n_heads * 2 * 4 + 255) / 256) * 256;
     out->slot_o = reinterpret_cast<float *>(b);

@@ -36,6 +36,8 @@ struct DecodeParams {
     uint32_t row_bytes;       // n_kv * D * sizeof(elem)
     float qscale;             // scale * log2(e)
     int mode;
+    int merge_in_kernel;      // 1: last CTA of a sequence merges its slots;
+                              // 0: slots are merged by launch_slot_merge
     DecodeSeq seqs[kMaxSeqsPerLaunch];
 };
 
@@ -50,6 +52,9 @@ struct DecodeWorkspace {
 
 size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
                               int num_sms);
+// Bytes at the start of a workspace that must be zero before a call
+// (error word and merge tickets).
+size_t decode_workspace_zero_bytes();
 bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads,
                             uint32_t head_dim, int num_sms, DecodeWorkspace *out);
 
@@ -61,6 +66,14 @@ uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv);
 // cudaErrorNotSupported.
 cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim,
                           uint32_t group, int grid, cudaStream_t stream);
+
+// Merge of split-K slots for sequences spread over more CTAs than the
+// in-kernel merge handles well; one CTA per (sequence, head) row.
+cudaError_t launch_slot_merge(const DecodeParams &p, uint32_t head_dim, cudaStream_t stream);
+
+// A sequence spanning more CTAs than this has its slots merged by
+// launch_slot_merge instead of by its last CTA.
+constexpr uint32_t kInKernelMergeMaxSlots = 8;
 
 cudaError_t launch_merge_lse(const float *m, const float *l, const float *o, uint32_t n_parts,
                              uint32_t n_rows, uint32_t head_dim, float *out,

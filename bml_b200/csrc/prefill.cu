@@ -310,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         for (uint32_t j = 0; j < n_tiles; ++j) {
             const uint32_t sb = j & 1u;
             mbar_wait(&s_full[sb], (j >> 1) & 1u, abort_flag, p.err);
+            __syncwarp();  // lanes leave the spin separately; tcgen05.ld needs the whole warp
             tc_fence_after();
             float s[BN];
 #pragma unroll
@@ -331,20 +332,39 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 for (int i = 0; i < BN; ++i)
                     if (kv0 + i >= p.S) s[i] = -INFINITY;
             }
-            float mx = s[0];
+            // row max: 8 independent chains (a single 128-long chain of
+            // dependent max operations would dominate the softmax time)
+            float mx8[8];
 #pragma unroll
-            for (int i = 1; i < BN; ++i) mx = fmaxf(mx, s[i]);
-            const float m_tile = mx * c;
+            for (int k = 0; k < 8; ++k) mx8[k] = s[k];
+#pragma unroll
+            for (int i = 8; i < BN; i += 8)
+#pragma unroll
+                for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], s[i + k]);
+#pragma unroll
+            for (int w = 4; w > 0; w >>= 1)
+#pragma unroll
+                for (int k = 0; k < w; ++k) mx8[k] = fmaxf(mx8[k], mx8[k + w]);
+            const float m_tile = mx8[0] * c;
             float m_new = m_run;
             if (m_run == -INFINITY || m_tile > m_run + kRescaleThreshold) m_new = fmaxf(m_run, m_tile);
             const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
             const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_use);
-            float sum = 0.f;
+            // p = 2^(s*c - m), summed in 4 independent packed f32x2 chains
+            const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
+            float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                              make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int i = 0; i < BN; ++i) {
-                s[i] = fast_exp2(fmaf(s[i], c, -m_use));
-                sum += s[i];
+            for (int i = 0; i < BN; i += 2) {
+                float2 x = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
+                x.x = fast_exp2(x.x);
+                x.y = fast_exp2(x.y);
+                s[i] = x.x;
+                s[i + 1] = x.y;
+                sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], x);
             }
+            const float2 sum2 = __fadd2_rn(__fadd2_rn(sum4[0], sum4[1]), __fadd2_rn(sum4[2], sum4[3]));
+            const float sum = sum2.x + sum2.y;
             l_run = l_run * alpha + sum;
             const bool rescale = (j > 0) && (m_new != m_run);
             m_run = m_new;
@@ -352,6 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             if (j > 0) {
                 // PV(j-1) must be done: it reads P, and O gets rescaled here
                 mbar_wait(o_done, (j - 1) & 1u, abort_flag, p.err);
+                __syncwarp();
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, rescale)) {
                     const float a = rescale ? alpha : 1.f;
@@ -401,6 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 
         // epilogue: O / l -> global
         mbar_wait(o_done, (n_tiles - 1) & 1u, abort_flag, p.err);
+        __syncwarp();
         tc_fence_after();
         const float inv_l = 1.f / l_run;
         const bool valid = t < p.S;

@@ -275,3 +275,38 @@ def test_gpu_softmax_f32(cuda):
     got = bml_b200.softmax_f32(to_dev(rows)).cpu().numpy()
     want = np.stack([oracle.softmax_f32(r) for r in rows])
     np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-9)
+
+
+def test_long_and_short_sequences_mixed(cuda):
+    """Long sequences span many CTAs (their split-K slots are merged by the
+    separate merge kernel) next to short ones handled by a single CTA."""
+    rng = np.random.default_rng(31)
+    lens = [60000, 3, 20000, 1, 129]
+    q = rng.standard_normal((len(lens), 32, 128), dtype=np.float32)
+    ks = [W.f32_to_bf16_bits(rng.standard_normal((L, 8, 128), dtype=np.float32)) for L in lens]
+    vs = [W.f32_to_bf16_bits(rng.standard_normal((L, 8, 128), dtype=np.float32)) for L in lens]
+    got = run_batched(q, ks, vs, code=oracle.BF16)
+    want = oracle.attn_decode_batched(q, ks, vs, dtype=oracle.BF16)
+    assert np.abs(got - want).max() < TOL
+
+
+def test_workspace_shared_by_calls_of_different_shapes(cuda):
+    """One workspace serves calls of any shape in any order: the merge
+    tickets sit at a fixed place, so leftover partials of one call never
+    read as tickets in the next."""
+    import bml_b200
+    ws = bml_b200.Workspace()
+    rng = np.random.default_rng(41)
+    cases = []
+    for lens, n_kv, G, d in (([4099, 1000, 3], 1, 8, 64), ([700] * 9 + [5000], 4, 8, 64),
+                             ([9000, 2], 8, 4, 128), ([300] * 40, 2, 2, 128)):
+        q = rng.standard_normal((len(lens), n_kv * G, d), dtype=np.float32)
+        ks = [rng.standard_normal((L, n_kv, d), dtype=np.float32).astype(np.float16) for L in lens]
+        vs = [rng.standard_normal((L, n_kv, d), dtype=np.float32).astype(np.float16) for L in lens]
+        cases.append((q, ks, vs, oracle.attn_decode_batched(q, ks, vs)))
+    for _ in range(2):
+        for q, ks, vs, want in cases:
+            got = bml_b200.decode_batched(to_dev(q), [to_dev(k) for k in ks], [to_dev(v) for v in vs],
+                                          workspace=ws).cpu().numpy()
+            assert np.abs(got - want).max() < TOL
+    ws.check()
