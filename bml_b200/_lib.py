@@ -76,6 +76,7 @@ SIGNATURES = {
     "bml_attn_prefill": (_st, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, C.c_int, C.c_float,
                                C.c_int, _vp, C.c_int, _vp]),
     "bml_softmax_f32": (_st, [_vp, _u32, _u32, _vp, _vp]),
+    "bml_diag_exp2": (_st, [_vp, _u32, C.c_int, _vp, _vp]),
     "bml_attn_workspace_check": (_st, [_vp, _sz, _vp]),
 }
 

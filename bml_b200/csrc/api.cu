@@ -584,6 +584,14 @@ BML_API bml_status bml_attn_prefill(const void *q_dev, const void *k_dev, const 
     return ok();
 }
 
+BML_API bml_status bml_diag_exp2(const float *x_dev, uint32_t n, int method, float *out_dev, void *stream) {
+    if (!x_dev || !out_dev || (n & 1u) || (method != 0 && method != 1))
+        return fail(BML_E_INVALID, "bml_diag_exp2: bad argument");
+    if (!aligned16(x_dev) || !aligned16(out_dev)) return fail(BML_E_INVALID, "bml_diag_exp2: alignment");
+    CUDA_TRY(bml::diag_exp2(x_dev, n, method, out_dev, static_cast<cudaStream_t>(stream)), "bml_diag_exp2");
+    return ok();
+}
+
 // ---------------------------------------------------------------------------
 // softmax_f32 (kv_cache.rs:188-200)
 // ---------------------------------------------------------------------------

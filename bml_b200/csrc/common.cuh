@@ -120,6 +120,38 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// max of three f32 values in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^x for a pair of values on the FMA and ALU pipes instead of the SFU,
+// for x in [-126, 126] (smaller x is clamped to 2^-126).  Method: Cody-Waite
+// range reduction x = j + f with j = round(x), f in [-0.5, 0.5] (the
+// rounding is done by adding 1.5*2^23, which also leaves j in the low
+// mantissa bits), then 2^f by a cubic with c0 = 1 whose other coefficients
+// were least-squares fitted for this library on Chebyshev nodes (max
+// relative error 1.0e-4 on [-0.5, 0.5]), and 2^j applied by adding j to
+// the exponent field.  Used for part of the softmax exponentials whose
+// results are rounded to 16 bits, where 1e-4 is far below the rounding.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    const float2 magic = make_float2(12582912.0f, 12582912.0f);
+    x.x = fmaxf(x.x, -126.0f);
+    x.y = fmaxf(x.y, -126.0f);
+    const float2 t = __fadd2_rn(x, magic);
+    const float2 jf = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = __ffma2_rn(jf, make_float2(-1.0f, -1.0f), x);
+    float2 p = __ffma2_rn(make_float2(0.05500892f, 0.05500892f), f, make_float2(0.24221097f, 0.24221097f));
+    p = __ffma2_rn(p, f, make_float2(0.69328290f, 0.69328290f));
+    p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+    float2 r;
+    r.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+    r.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+    return r;
+}
+
 // ---------------------------------------------------------------------------
 // 16-byte chunk -> f32 lanes, per storage dtype.
 // ---------------------------------------------------------------------------

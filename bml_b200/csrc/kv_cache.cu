@@ -111,7 +111,22 @@ __global__ void softmax_kernel(const float *__restrict__ x, uint32_t n, float *_
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) orow[i] = ok ? orow[i] / sum : inv_n;
 }
 
+__global__ void diag_exp2_kernel(const float2 *__restrict__ x, uint32_t n2, int method, float2 *__restrict__ out) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n2) return;
+    const float2 v = x[i];
+    out[i] = method == 1 ? exp2_poly2(v) : make_float2(fast_exp2(v.x), fast_exp2(v.y));
+}
+
 }  // namespace
+
+cudaError_t diag_exp2(const float *x, uint32_t n, int method, float *out, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const uint32_t n2 = n / 2;
+    diag_exp2_kernel<<<(n2 + 255) / 256, 256, 0, st>>>(reinterpret_cast<const float2 *>(x), n2, method,
+                                                        reinterpret_cast<float2 *>(out));
+    return cudaGetLastError();
+}
 
 cudaError_t kv_store_from_f32(const float *src_dev, void *dst_dev, bml_dtype dst_t, size_t n,
                               cudaStream_t st) {

@@ -11,6 +11,7 @@ cudaError_t kv_convert(const void *src_dev, bml_dtype src_t, void *dst_dev, bml_
                        cudaStream_t st);
 cudaError_t kv_dot(const float *q_dev, const void *k_dev, bml_dtype t, uint32_t n, float *out_dev,
                    cudaStream_t st);
+cudaError_t diag_exp2(const float *x, uint32_t n, int method, float *out, cudaStream_t st);
 cudaError_t softmax_rows(const float *x_dev, uint32_t n_rows, uint32_t n, float *out_dev, cudaStream_t st);
 
 }  // namespace bml

@@ -35,7 +35,7 @@ namespace {
 
 constexpr int BM = 128;  // query rows per CTA (TMEM lanes)
 constexpr int BN = 128;  // kv positions per tile
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer, MMA issuer, 8 softmax warps
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int D>
@@ -50,7 +50,9 @@ struct PCfg {
     static constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
     static constexpr int OFF_P = OFF_V + STAGES * TILE_BYTES;
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
-    static constexpr int SMEM = OFF_BAR + 256 + 1024;  // + alignment slack
+    // row-max exchange [2 buffers][2 halves][BM] + row-sum exchange [2 halves][BM]
+    static constexpr int OFF_X = OFF_BAR + 256;
+    static constexpr int SMEM = OFF_X + 3 * 2 * BM * 4 + 1024;  // + alignment slack
     static constexpr uint32_t S_COL = 0;    // two S buffers: columns [0,128), [128,256)
     static constexpr uint32_t O_COL = 256;  // O: columns [256, 256+D)
     static constexpr uint32_t TMEM_COLS = 512;
@@ -205,9 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], 4);
+            mbar_init(&s_empty[i], 8);
         }
-        mbar_init(p_full, 4);
+        mbar_init(p_full, 8);
         mbar_init(o_done, 1);
         misc[1] = 0u;
         fence_mbar_init();
@@ -299,73 +301,87 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         __syncwarp();
     } else {
         // ------------------------------------------------------------- softmax
+        // Two warps share each TMEM lane quarter: warp w owns rows
+        // 32*(w%4) .. +31 and the column half hf of every S row (and of O);
+        // the pair exchanges its half-row maxima once per tile.
         const uint32_t q4 = warp & 3;            // TMEM lane quarter of this warp
+        const uint32_t hf = (warp - 2) >> 2;     // column half: 0 for warps 2-5, 1 for 6-9
         const uint32_t r = q4 * 32 + lane;       // query row within the tile
         const uint32_t t = q0 + r;               // query position
         const uint32_t lane_addr = (q4 * 32) << 16;
+        constexpr int HC = BN / 2;               // score columns per thread
+        constexpr int HD = D / 2;                // output columns per thread
+        float *xch = reinterpret_cast<float *>(smem + C::OFF_X);  // [buf][half][row]
         const float c = p.scale_log2;
-        float m_run = -INFINITY, l_run = 0.f;
-        uint8_t *prow = sP + (r >> 3) * 1024 + (r & 7) * 128;
+        float m_run = -INFINITY, l_part = 0.f;
+        uint8_t *prow = sP + (r >> 3) * 1024 + (r & 7) * 128 + hf * (BM * 128);
 
         for (uint32_t j = 0; j < n_tiles; ++j) {
             const uint32_t sb = j & 1u;
             mbar_wait(&s_full[sb], (j >> 1) & 1u, abort_flag, p.err);
             __syncwarp();  // lanes leave the spin separately; tcgen05.ld needs the whole warp
             tc_fence_after();
-            float s[BN];
+            float s[HC];
 #pragma unroll
-            for (int cc = 0; cc < BN / 32; ++cc) tmem_ld32(tmem + lane_addr + C::S_COL + sb * BN + cc * 32, s + cc * 32);
+            for (int cc = 0; cc < HC / 32; ++cc)
+                tmem_ld32(tmem + lane_addr + C::S_COL + sb * BN + hf * HC + cc * 32, s + cc * 32);
             tmem_wait_ld();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[sb]);
 
-            const uint32_t kv0 = j * BN;
+            const uint32_t kv0 = j * BN + hf * HC;   // key position of s[0]
             if (p.causal) {
-                if (kv0 + BN - 1 > t) {
+                if (kv0 + HC - 1 > t) {
 #pragma unroll
-                    for (int i = 0; i < BN; ++i)
+                    for (int i = 0; i < HC; ++i)
                         if (kv0 + i > t) s[i] = -INFINITY;
                 }
-            } else if (kv0 + BN > p.S) {
+            } else if (kv0 + HC > p.S) {
 #pragma unroll
-                for (int i = 0; i < BN; ++i)
+                for (int i = 0; i < HC; ++i)
                     if (kv0 + i >= p.S) s[i] = -INFINITY;
             }
-            // row max: 8 independent chains (a single 128-long chain of
-            // dependent max operations would dominate the softmax time)
+            // half-row max: 8 chains of three-input max over 64 columns
             float mx8[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) mx8[k] = s[k];
+            for (int k = 0; k < 8; ++k) {
+                float a = fmax3(s[k], s[k + 8], s[k + 16]);
 #pragma unroll
-            for (int i = 8; i < BN; i += 8)
-#pragma unroll
-                for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], s[i + k]);
-#pragma unroll
-            for (int w = 4; w > 0; w >>= 1)
-#pragma unroll
-                for (int k = 0; k < w; ++k) mx8[k] = fmaxf(mx8[k], mx8[k + w]);
-            const float m_tile = mx8[0] * c;
+                for (int i = 24; i + 8 < HC; i += 16) a = fmax3(a, s[k + i], s[k + i + 8]);  // up to k+48
+                mx8[k] = fmaxf(a, s[k + HC - 8]);                                           // k+56
+            }
+            float mh = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+            // exchange with the partner warp (double-buffered by tile parity)
+            xch[(sb * 2 + hf) * BM + r] = mh;
+            __syncwarp();
+            named_bar_sync(2 + q4, 64);
+            mh = fmaxf(mh, xch[(sb * 2 + (hf ^ 1u)) * BM + r]);
+            const float m_tile = mh * c;
             float m_new = m_run;
             if (m_run == -INFINITY || m_tile > m_run + kRescaleThreshold) m_new = fmaxf(m_run, m_tile);
             const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
             const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_use);
-            // p = 2^(s*c - m), summed in 4 independent packed f32x2 chains
+            // p = 2^(s*c - m): one pair in four on the FMA/ALU pipes, the rest
+            // on the SFU; summed in 4 independent packed chains
             const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
             float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                               make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int i = 0; i < BN; i += 2) {
+            for (int i = 0; i < HC; i += 2) {
                 float2 x = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
-                x.x = fast_exp2(x.x);
-                x.y = fast_exp2(x.y);
+                if (((i >> 1) & 3) == 3) {
+                    x = exp2_poly2(x);
+                } else {
+                    x.x = fast_exp2(x.x);
+                    x.y = fast_exp2(x.y);
+                }
                 s[i] = x.x;
                 s[i + 1] = x.y;
                 sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], x);
             }
             const float2 sum2 = __fadd2_rn(__fadd2_rn(sum4[0], sum4[1]), __fadd2_rn(sum4[2], sum4[3]));
-            const float sum = sum2.x + sum2.y;
-            l_run = l_run * alpha + sum;
+            l_part = l_part * alpha + (sum2.x + sum2.y);
             const bool rescale = (j > 0) && (m_new != m_run);
             m_run = m_new;
 
@@ -377,21 +393,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 if (__any_sync(0xffffffffu, rescale)) {
                     const float a = rescale ? alpha : 1.f;
 #pragma unroll
-                    for (int cc = 0; cc < D / 32; ++cc) {
+                    for (int cc = 0; cc < HD / 32; ++cc) {
                         float o[32];
-                        tmem_ld32(tmem + lane_addr + C::O_COL + cc * 32, o);
+                        tmem_ld32(tmem + lane_addr + C::O_COL + hf * HD + cc * 32, o);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 32; ++i) o[i] *= a;
-                        tmem_st32(tmem + lane_addr + C::O_COL + cc * 32, o);
+                        tmem_st32(tmem + lane_addr + C::O_COL + hf * HD + cc * 32, o);
                     }
                     tmem_wait_st();
                 }
             }
-            // P row -> shared memory, 128B-swizzled K-major layout
+            // P half-row -> shared memory (column block hf), 128B-swizzled K-major
 #pragma unroll
-            for (int ch = 0; ch < BN / 8; ++ch) {
-                const int kb = ch >> 3, cw = ch & 7;
+            for (int ch = 0; ch < HC / 8; ++ch) {
                 uint4 pk;
                 if (kF16) {
                     __half2 h0 = __floats2half2_rn(s[ch * 8 + 0], s[ch * 8 + 1]);
@@ -412,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     pk.z = *reinterpret_cast<uint32_t *>(&h2);
                     pk.w = *reinterpret_cast<uint32_t *>(&h3);
                 }
-                *reinterpret_cast<uint4 *>(prow + kb * (BM * 128) + ((cw ^ (r & 7)) << 4)) = pk;
+                *reinterpret_cast<uint4 *>(prow + ((ch ^ (r & 7)) << 4)) = pk;
             }
             fence_proxy_async_smem();
             tc_fence_before();
@@ -420,17 +435,20 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             if (lane == 0) mbar_arrive(p_full);
         }
 
-        // epilogue: O / l -> global
+        // epilogue: l = both halves' partial sums; O / l -> global
+        xch[(4 + hf) * BM + r] = l_part;  // its own buffer: the partner may still read a max slot
         mbar_wait(o_done, (n_tiles - 1) & 1u, abort_flag, p.err);
         __syncwarp();
+        named_bar_sync(2 + q4, 64);
+        const float l_row = l_part + xch[(4 + (hf ^ 1u)) * BM + r];
         tc_fence_after();
-        const float inv_l = 1.f / l_run;
+        const float inv_l = 1.f / l_row;
         const bool valid = t < p.S;
-        const size_t orow = ((size_t)(row_base + t) * p.H + h) * D;
+        const size_t orow = ((size_t)(row_base + t) * p.H + h) * D + hf * HD;
 #pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
+        for (int cc = 0; cc < HD / 32; ++cc) {
             float o[32];
-            tmem_ld32(tmem + lane_addr + C::O_COL + cc * 32, o);
+            tmem_ld32(tmem + lane_addr + C::O_COL + hf * HD + cc * 32, o);
             tmem_wait_ld();
             if (valid) {
                 if (p.out_f32) {

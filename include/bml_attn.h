@@ -275,6 +275,18 @@ bml_status bml_softmax_f32(const float *x_dev, uint32_t n_rows, uint32_t n,
                            float *out_dev, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* Diagnostics                                                              */
+/* ------------------------------------------------------------------------ */
+
+/* Evaluates 2^x with one of the device exponentials the attention kernels
+ * use, so tests can bound their error: method 0 = the SFU (ex2.approx),
+ * method 1 = the FMA-pipe polynomial the prefill softmax uses for part of
+ * its exponentials.  No reference counterpart.  n must be even.
+ * Asynchronous. */
+bml_status bml_diag_exp2(const float *x_dev, uint32_t n, int method,
+                         float *out_dev, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Device-side error word                                                   */
 /* ------------------------------------------------------------------------ */
 

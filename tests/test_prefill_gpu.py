@@ -119,3 +119,19 @@ def test_prefill_bf16_output_and_repeat(cuda):
     torch.cuda.synchronize()
     assert torch.equal(a, b), "prefill is deterministic"
     assert (c.float() - a).abs().max().item() < 1e-2
+
+
+@pytest.mark.parametrize("method,bound", [(0, 2e-6), (1, 1.2e-4)])
+def test_device_exp2_error_bounds(cuda, method, bound):
+    """The device exponentials of the softmax against CUDA's exp2f: the SFU
+    form (ex2.approx) and the FMA-pipe cubic (Cody-Waite reduction) that
+    replaces one SFU exponential in four in the prefill softmax."""
+    import ctypes as C
+    import bml_b200._lib as L
+    x = torch.linspace(-125.5, 10.0, 200002, device="cuda", dtype=torch.float32)
+    out = torch.empty_like(x)
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert L.lib().bml_diag_exp2(C.c_void_p(x.data_ptr()), x.numel(), method, C.c_void_p(out.data_ptr()), st) == 0
+    want = torch.exp2(x.double())
+    rel = ((out.double() - want).abs() / want).max().item()
+    assert rel < bound, rel
