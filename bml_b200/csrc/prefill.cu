@@ -7,21 +7,29 @@
 // time.  Here the whole prompt runs at once as a flash-attention kernel:
 // bf16/f16 operands, f32 accumulation, online softmax.
 //
-// One CTA handles 128 query rows of one (sequence, q head).  Warp roles:
-//   warp 0      TMA producer: Q once, then K and V tiles of 128 positions
-//               into a multi-stage ring (cp.async.bulk.tensor, 128B swizzle,
-//               no multicast), completing on mbarriers.
-//   warp 1      allocates tensor memory; lane 0 issues every tcgen05.mma:
-//               S = Q K^T into one of two TMEM S buffers, and O += P V into
-//               the TMEM O accumulator; tcgen05.commit signals completion.
-//   warps 2-5   softmax: thread r owns query row r (TMEM lane r).  It reads
-//               its S row with tcgen05.ld, applies the causal mask, keeps the
-//               running max / sum, writes P (bf16) into 128B-swizzled shared
-//               memory for the next MMA, and rescales O in TMEM only when its
-//               running max grew by more than 2^8 (the final O / l is exact
-//               for any fixed reference max).  At the end it divides O by l.
-// The MMA warp issues S(j+1) = Q K(j+1)^T before waiting for P(j), so the
-// tensor core computes the next scores while the softmax warps work.
+// One CTA handles two consecutive 128-row query tiles, A and B, of one
+// (sequence, q head).  Both read the same K/V tiles, so every K/V tile in
+// shared memory feeds twice the tensor-core work, and while the softmax of
+// one tile runs the tensor core works on the other.  Tensor memory (512
+// columns) holds S_A, S_B (128 columns each) and the accumulators O_A, O_B.
+// Warp roles:
+//   warp 0      TMA producer: Q_A and Q_B once, then K and V tiles of 128
+//               positions into a stage ring (cp.async.bulk.tensor, 128B
+//               swizzle, no multicast), completing on mbarriers.
+//   warp 1      allocates tensor memory; lane 0 issues every tcgen05.mma.
+//   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: thread r
+//               owns query row r (TMEM lane r).  It reads its S row in two
+//               passes over tensor memory (row max, then exponentials),
+//               writes P back over S as packed 16-bit pairs with tcgen05.st,
+//               and rescales O in TMEM only when its running max grew by
+//               more than 2^8 (the final O / l is exact for any fixed
+//               reference max).
+// P.V takes P straight from tensor memory (tcgen05.mma with the A operand in
+// TMEM) and V from shared memory.  The MMA issue order per K/V tile j is
+// PV_A(j), S_A(j+1), PV_B(j), S_B(j+1).  Tensor-core operations of one
+// thread run in issue order, so S_X(j+1) overwrites P_X(j) only after PV_X(j)
+// has read it, and the commit that announces S_X(j+1) also tells the softmax
+// that PV_X(j) has finished: O_X may be rescaled and P_X rewritten.
 #include <cudaTypedefs.h>
 #include <math.h>
 
@@ -33,36 +41,37 @@ namespace bml {
 
 namespace {
 
-constexpr int BM = 128;  // query rows per CTA (TMEM lanes)
+constexpr int BM = 128;  // query rows per tile (TMEM lanes)
 constexpr int BN = 128;  // kv positions per tile
-constexpr int kThreads = 320;  // producer, MMA issuer, 8 softmax warps
+constexpr int kThreads = 320;  // producer, MMA issuer, 4 + 4 softmax warps
+constexpr int kMaxStages = 4;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int D>
 struct PCfg {
     static constexpr int KB = D / 64;                // 128-byte column blocks of a row
-    static constexpr int Q_BYTES = BM * D * 2;
-    static constexpr int TILE_BYTES = BN * D * 2;
-    static constexpr int P_BYTES = BM * BN * 2;
-    static constexpr int STAGES = D == 128 ? 2 : 3;
-    static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = OFF_Q + Q_BYTES;
+    static constexpr int Q_BYTES = BM * D * 2;       // one Q tile
+    static constexpr int TILE_BYTES = BN * D * 2;    // one K or V tile
+    static constexpr int STAGES = D == 128 ? 2 : 4;
+    static constexpr int OFF_Q = 0;                  // Q_A, Q_B
+    static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
     static constexpr int OFF_V = OFF_K + STAGES * TILE_BYTES;
-    static constexpr int OFF_P = OFF_V + STAGES * TILE_BYTES;
-    static constexpr int OFF_BAR = OFF_P + P_BYTES;
-    // row-max exchange [2 buffers][2 halves][BM] + row-sum exchange [2 halves][BM]
-    static constexpr int OFF_X = OFF_BAR + 256;
-    static constexpr int SMEM = OFF_X + 3 * 2 * BM * 4 + 1024;  // + alignment slack
-    static constexpr uint32_t S_COL = 0;    // two S buffers: columns [0,128), [128,256)
-    static constexpr uint32_t O_COL = 256;  // O: columns [256, 256+D)
+    static constexpr int OFF_BAR = OFF_V + STAGES * TILE_BYTES;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;  // + alignment slack
+    // tensor memory: S_x at x*128 (P_x aliases its first 64 columns),
+    // O_x at 256 + x*D
+    static constexpr uint32_t O_COL0 = 256;
     static constexpr uint32_t TMEM_COLS = 512;
 };
+static_assert(PCfg<128>::SMEM <= 227 * 1024, "shared memory");
+static_assert(PCfg<64>::SMEM <= 227 * 1024, "shared memory");
+static_assert(PCfg<64>::STAGES <= kMaxStages && PCfg<128>::STAGES <= kMaxStages, "stages");
 
 struct PrefillParams {
     CUtensorMap tq, tk, tv;  // 3-D maps (d, heads, n_seqs*seq_len), box (64, 1, 128)
     void *out;
     uint32_t *err;
-    uint32_t S, H, Hkv, n_seqs, n_mtiles;
+    uint32_t S, H, Hkv, n_seqs, n_mtiles, n_pairs;
     float scale_log2;  // scale * log2(e)
     int causal;
     int out_f32;
@@ -106,7 +115,19 @@ __device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint
         : "memory");
 }
 
-// 32 consecutive f32 columns of this thread's TMEM lane.
+// D[tmem] (+)= A[tmem] * B[smem desc]; A is M x 16 with two 16-bit
+// elements per 32-bit column (8 columns per instruction).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 consecutive 32-bit columns of this thread's TMEM lane.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
     uint32_t r[32];
     asm volatile(
@@ -142,12 +163,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
         : "memory");
 }
 
+// 16 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *w) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15, %16};" ::"r"(taddr),
+        "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7]), "r"(w[8]),
+        "r"(w[9]), "r"(w[10]), "r"(w[11]), "r"(w[12]), "r"(w[13]), "r"(w[14]), "r"(w[15])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // Shared-memory matrix descriptor, 128B swizzle, sm_100 version bits.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -158,6 +185,17 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 // Instruction descriptor for kind::f16: f32 accumulate, A K-major.
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t in_fmt, uint32_t m, uint32_t n, uint32_t b_mn_major) {
     return (1u << 4) | (in_fmt << 7) | (in_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// two f32 -> one 32-bit word of 16-bit values, lo in the low half
+template <bool kF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    if (kF16) {
+        __half2 h = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
 }
 
 // ----------------------------------------------------------------- kernel
@@ -171,30 +209,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     uint8_t *sQ = smem + C::OFF_Q;
     uint8_t *sK = smem + C::OFF_K;
     uint8_t *sV = smem + C::OFF_V;
-    uint8_t *sP = smem + C::OFF_P;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::OFF_BAR);
-    uint64_t *q_full = bars;
-    uint64_t *k_full = bars + 1;
-    uint64_t *k_empty = k_full + C::STAGES;
-    uint64_t *v_full = k_empty + C::STAGES;
-    uint64_t *v_empty = v_full + C::STAGES;
-    uint64_t *s_full = v_empty + C::STAGES;  // [2]
-    uint64_t *s_empty = s_full + 2;          // [2]
-    uint64_t *p_full = s_empty + 2;
-    uint64_t *o_done = p_full + 1;
-    volatile uint32_t *misc = reinterpret_cast<volatile uint32_t *>(o_done + 1);  // [0] tmem base, [1] abort
+    uint64_t *q_full = bars;                    // Q_A and Q_B landed
+    uint64_t *k_full = bars + 1;                // [stage]
+    uint64_t *k_empty = k_full + kMaxStages;    // [stage]
+    uint64_t *v_full = k_empty + kMaxStages;    // [stage]
+    uint64_t *v_empty = v_full + kMaxStages;    // [stage]
+    uint64_t *s_full = v_empty + kMaxStages;    // [chain]: S of the chain's current tile in TMEM
+    uint64_t *p_full = s_full + 2;              // [chain]: P of the chain's current tile in TMEM
+    uint64_t *o_final = p_full + 2;             // [chain]: last P.V of the chain done
+    volatile uint32_t *misc = reinterpret_cast<volatile uint32_t *>(o_final + 2);  // [0] tmem base, [1] abort
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // work unit: heaviest (last) query tiles first
+    // work unit: heaviest (last) tile pairs first
     const uint32_t per = p.n_seqs * p.H;
-    const uint32_t mt = p.n_mtiles - 1 - blockIdx.x / per;
+    const uint32_t pair = p.n_pairs - 1 - blockIdx.x / per;
     const uint32_t bh = blockIdx.x % per;
     const uint32_t b = bh / p.H, h = bh % p.H;
     const uint32_t hk = h / (p.H / p.Hkv);
-    const uint32_t q0 = mt * BM;
     const uint32_t kv_tiles_all = (p.S + BN - 1) / BN;
-    const uint32_t n_tiles = p.causal ? min(kv_tiles_all, (q0 + BM - 1) / BN + 1) : kv_tiles_all;
+    // Query tile of each chain and its number of K/V tiles.  BM == BN, so
+    // causally tile m sees K/V tiles 0..m.  nt1 >= nt0: chain B is always
+    // the last user of a K/V stage.  (With an odd tile count the last pair's
+    // tile B lies past the prompt; it runs on whatever rows the map returns
+    // and writes nothing.)
+    const uint32_t mt0 = 2 * pair, mt1 = 2 * pair + 1;
+    const uint32_t nt0 = p.causal ? min(kv_tiles_all, mt0 + 1) : kv_tiles_all;
+    const uint32_t nt1 = p.causal ? min(kv_tiles_all, mt1 + 1) : kv_tiles_all;
     const int row_base = (int)(b * p.S);
 
     if (threadIdx.x == 0) {
@@ -205,12 +247,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_empty[i], 8);
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(&s_full[x], 1);
+            mbar_init(&p_full[x], 4);
+            mbar_init(&o_final[x], 1);
         }
-        mbar_init(p_full, 8);
-        mbar_init(o_done, 1);
         misc[1] = 0u;
         fence_mbar_init();
     }
@@ -235,11 +276,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     if (warp == 0) {
         // ------------------------------------------------------------- TMA producer
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+            mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
 #pragma unroll
-            for (int kb = 0; kb < C::KB; ++kb)
-                tma_load_3d(sQ + kb * BM * 128, &p.tq, kb * 64, (int)h, row_base + (int)q0, q_full);
-            for (uint32_t j = 0; j < n_tiles; ++j) {
+            for (int x = 0; x < 2; ++x)
+#pragma unroll
+                for (int kb = 0; kb < C::KB; ++kb)
+                    tma_load_3d(sQ + x * C::Q_BYTES + kb * BM * 128, &p.tq, kb * 64, (int)h,
+                                row_base + (int)((x ? mt1 : mt0) * BM), q_full);
+            for (uint32_t j = 0; j < nt1; ++j) {
                 const uint32_t st = j % C::STAGES, u = j / C::STAGES;
                 const int row = row_base + (int)(j * BN);
                 if (j >= (uint32_t)C::STAGES) mbar_wait(&k_empty[st], (u & 1u) ^ 1u, abort_flag, p.err);
@@ -261,194 +305,173 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             constexpr uint32_t fmt = kF16 ? 0u : 1u;
             constexpr uint32_t idesc_qk = make_idesc(fmt, BM, BN, 0);
             constexpr uint32_t idesc_pv = make_idesc(fmt, BM, D, 1);
-            const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV),
-                           p_base = smem_u32(sP);
+            const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
             mbar_wait(q_full, 0, abort_flag, p.err);
-            auto issue_qk = [&](uint32_t j) {
-                const uint32_t st = j % C::STAGES, sb = j & 1u;
-                mbar_wait(&k_full[st], (j / C::STAGES) & 1u, abort_flag, p.err);
-                if (j >= 2) mbar_wait(&s_empty[sb], ((j >> 1) & 1u) ^ 1u, abort_flag, p.err);
-                tc_fence_after();
+            // S_x = Q_x K(j)^T.  The first chain to use K(j) waits for it;
+            // chain B, the last user, releases the stage.
+            auto issue_qk = [&](uint32_t x, uint32_t j) {
+                const uint32_t st = j % C::STAGES;
+                if (x == 0 || j >= nt0) {
+                    mbar_wait(&k_full[st], (j / C::STAGES) & 1u, abort_flag, p.err);
+                    tc_fence_after();
+                }
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+                    const uint32_t off = x * C::Q_BYTES + (kk >> 2) * (BM * 128) + (kk & 3) * 32;
                     const uint32_t koff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-                    tc_mma_ss(tmem + C::S_COL + sb * BN, smem_desc(q_base + off, 16, 1024),
+                    tc_mma_ss(tmem + x * 128, smem_desc(q_base + off, 16, 1024),
                               smem_desc(k_base + st * C::TILE_BYTES + koff, 16, 1024), idesc_qk, kk > 0);
                 }
-                tc_commit(&s_full[sb]);
-                tc_commit(&k_empty[st]);
+                tc_commit(&s_full[x]);
+                if (x == 1) tc_commit(&k_empty[st]);
             };
-            issue_qk(0);
-            for (uint32_t j = 0; j < n_tiles; ++j) {
-                if (j + 1 < n_tiles) issue_qk(j + 1);
+            // O_x += P_x V(j), P_x read from tensor memory (over S_x)
+            auto issue_pv = [&](uint32_t x, uint32_t j) {
                 const uint32_t st = j % C::STAGES;
-                mbar_wait(p_full, j & 1u, abort_flag, p.err);
-                mbar_wait(&v_full[st], (j / C::STAGES) & 1u, abort_flag, p.err);
+                mbar_wait(&p_full[x], j & 1u, abort_flag, p.err);
+                if (x == 0 || j >= nt0) mbar_wait(&v_full[st], (j / C::STAGES) & 1u, abort_flag, p.err);
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint32_t poff = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
                     const uint32_t voff = kk * 16 * 128;  // 16 kv rows of 128 B
-                    tc_mma_ss(tmem + C::O_COL, smem_desc(p_base + poff, 16, 1024),
+                    tc_mma_ts(tmem + C::O_COL0 + x * D, tmem + x * 128 + kk * 8,
                               smem_desc(v_base + st * C::TILE_BYTES + voff, BN * 128, 1024), idesc_pv,
                               (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                tc_commit(o_done);
-                tc_commit(&v_empty[st]);
+                if (x == 1) tc_commit(&v_empty[st]);
+                if (j + 1 == (x ? nt1 : nt0)) tc_commit(&o_final[x]);
+            };
+            issue_qk(0, 0);
+            issue_qk(1, 0);
+            for (uint32_t j = 0; j < nt1; ++j) {
+                if (j < nt0) {
+                    issue_pv(0, j);
+                    if (j + 1 < nt0) issue_qk(0, j + 1);
+                }
+                issue_pv(1, j);
+                if (j + 1 < nt1) issue_qk(1, j + 1);
             }
         }
         __syncwarp();
     } else {
         // ------------------------------------------------------------- softmax
-        // Two warps share each TMEM lane quarter: warp w owns rows
-        // 32*(w%4) .. +31 and the column half hf of every S row (and of O);
-        // the pair exchanges its half-row maxima once per tile.
-        const uint32_t q4 = warp & 3;            // TMEM lane quarter of this warp
-        const uint32_t hf = (warp - 2) >> 2;     // column half: 0 for warps 2-5, 1 for 6-9
-        const uint32_t r = q4 * 32 + lane;       // query row within the tile
-        const uint32_t t = q0 + r;               // query position
+        const uint32_t x = (uint32_t)(warp - 2) >> 2;  // chain: 0 = tile A (warps 2-5), 1 = tile B (6-9)
+        const uint32_t q4 = warp & 3;                   // TMEM lane quarter of this warp
+        const uint32_t r = q4 * 32 + lane;              // query row within the tile
+        const uint32_t t = (x ? mt1 : mt0) * BM + r;    // query position
+        const uint32_t nt = x ? nt1 : nt0;
         const uint32_t lane_addr = (q4 * 32) << 16;
-        constexpr int HC = BN / 2;               // score columns per thread
-        constexpr int HD = D / 2;                // output columns per thread
-        float *xch = reinterpret_cast<float *>(smem + C::OFF_X);  // [buf][half][row]
+        const uint32_t s_col = tmem + lane_addr + x * 128;
+        const uint32_t o_col = tmem + lane_addr + C::O_COL0 + x * D;
         const float c = p.scale_log2;
-        float m_run = -INFINITY, l_part = 0.f;
-        uint8_t *prow = sP + (r >> 3) * 1024 + (r & 7) * 128 + hf * (BM * 128);
+        const uint32_t lim = p.causal ? t : p.S - 1;  // last key this row sees
+        float m_run = -INFINITY, l_run = 0.f;
 
-        for (uint32_t j = 0; j < n_tiles; ++j) {
-            const uint32_t sb = j & 1u;
-            mbar_wait(&s_full[sb], (j >> 1) & 1u, abort_flag, p.err);
+        for (uint32_t j = 0; j < nt; ++j) {
+            mbar_wait(&s_full[x], j & 1u, abort_flag, p.err);
             __syncwarp();  // lanes leave the spin separately; tcgen05.ld needs the whole warp
             tc_fence_after();
-            float s[HC];
-#pragma unroll
-            for (int cc = 0; cc < HC / 32; ++cc)
-                tmem_ld32(tmem + lane_addr + C::S_COL + sb * BN + hf * HC + cc * 32, s + cc * 32);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[sb]);
+            const uint32_t kv0 = j * BN;
+            const bool mask_tile = kv0 + BN - 1 > lim;
 
-            const uint32_t kv0 = j * BN + hf * HC;   // key position of s[0]
-            if (p.causal) {
-                if (kv0 + HC - 1 > t) {
+            // pass 1: row max, 8 chains of three-input max per 64 columns
+            float mh = -INFINITY;
 #pragma unroll
-                    for (int i = 0; i < HC; ++i)
-                        if (kv0 + i > t) s[i] = -INFINITY;
+            for (int half = 0; half < 2; ++half) {
+                float s[64];
+                tmem_ld32(s_col + half * 64, s);
+                tmem_ld32(s_col + half * 64 + 32, s + 32);
+                tmem_wait_ld();
+                if (mask_tile) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i)
+                        if (kv0 + half * 64 + i > lim) s[i] = -INFINITY;
                 }
-            } else if (kv0 + HC > p.S) {
+                float mx8[8];
 #pragma unroll
-                for (int i = 0; i < HC; ++i)
-                    if (kv0 + i >= p.S) s[i] = -INFINITY;
+                for (int k = 0; k < 8; ++k) {
+                    float a = fmax3(s[k], s[k + 8], s[k + 16]);
+                    a = fmax3(a, s[k + 24], s[k + 32]);
+                    a = fmax3(a, s[k + 40], s[k + 48]);
+                    mx8[k] = fmaxf(a, s[k + 56]);
+                }
+                mh = fmax3(mh, fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]));
+                mh = fmax3(mh, mx8[6], mx8[7]);
             }
-            // half-row max: 8 chains of three-input max over 64 columns
-            float mx8[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                float a = fmax3(s[k], s[k + 8], s[k + 16]);
-#pragma unroll
-                for (int i = 24; i + 8 < HC; i += 16) a = fmax3(a, s[k + i], s[k + i + 8]);  // up to k+48
-                mx8[k] = fmaxf(a, s[k + HC - 8]);                                           // k+56
-            }
-            float mh = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
-            // exchange with the partner warp (double-buffered by tile parity)
-            xch[(sb * 2 + hf) * BM + r] = mh;
-            __syncwarp();
-            named_bar_sync(2 + q4, 64);
-            mh = fmaxf(mh, xch[(sb * 2 + (hf ^ 1u)) * BM + r]);
             const float m_tile = mh * c;
             float m_new = m_run;
             if (m_run == -INFINITY || m_tile > m_run + kRescaleThreshold) m_new = fmaxf(m_run, m_tile);
             const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
             const float alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_use);
-            // p = 2^(s*c - m): one pair in four on the FMA/ALU pipes, the rest
-            // on the SFU; summed in 4 independent packed chains
+            const bool rescale = (j > 0) && (m_new != m_run);
+            m_run = m_new;
+
+            // O rescale (rare).  PV_x(j-1) has finished: S_x(j) was issued
+            // after it and its commit covers every earlier MMA.
+            if (__any_sync(0xffffffffu, rescale)) {
+                const float a = rescale ? alpha : 1.f;
+#pragma unroll
+                for (int cc = 0; cc < D / 32; ++cc) {
+                    float o[32];
+                    tmem_ld32(o_col + cc * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] *= a;
+                    tmem_st32(o_col + cc * 32, o);
+                }
+            }
+
+            // pass 2: p = 2^(s*c - m), 32 columns at a time, written back as
+            // packed 16-bit pairs over columns already read: P chunk q goes to
+            // columns 16q..16q+15, S chunk q came from 32q..32q+31.  One pair
+            // in four of the exponentials runs on the FMA/ALU pipes.
             const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
             float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                               make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int i = 0; i < HC; i += 2) {
-                float2 x = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
-                if (((i >> 1) & 3) == 3) {
-                    x = exp2_poly2(x);
-                } else {
-                    x.x = fast_exp2(x.x);
-                    x.y = fast_exp2(x.y);
+            for (int qc = 0; qc < BN / 32; ++qc) {
+                float s[32];
+                tmem_ld32(s_col + qc * 32, s);
+                tmem_wait_ld();
+                if (mask_tile) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (kv0 + qc * 32 + i > lim) s[i] = -INFINITY;
                 }
-                s[i] = x.x;
-                s[i + 1] = x.y;
-                sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], x);
+                uint32_t w[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    float2 e = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
+                    if (((i >> 1) & 3) == 3) {
+                        e = exp2_poly2(e);
+                    } else {
+                        e.x = fast_exp2(e.x);
+                        e.y = fast_exp2(e.y);
+                    }
+                    sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], e);
+                    w[i >> 1] = pack2<kF16>(e.x, e.y);
+                }
+                tmem_st16(s_col + qc * 16, w);
             }
             const float2 sum2 = __fadd2_rn(__fadd2_rn(sum4[0], sum4[1]), __fadd2_rn(sum4[2], sum4[3]));
-            l_part = l_part * alpha + (sum2.x + sum2.y);
-            const bool rescale = (j > 0) && (m_new != m_run);
-            m_run = m_new;
-
-            if (j > 0) {
-                // PV(j-1) must be done: it reads P, and O gets rescaled here
-                mbar_wait(o_done, (j - 1) & 1u, abort_flag, p.err);
-                __syncwarp();
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, rescale)) {
-                    const float a = rescale ? alpha : 1.f;
-#pragma unroll
-                    for (int cc = 0; cc < HD / 32; ++cc) {
-                        float o[32];
-                        tmem_ld32(tmem + lane_addr + C::O_COL + hf * HD + cc * 32, o);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) o[i] *= a;
-                        tmem_st32(tmem + lane_addr + C::O_COL + hf * HD + cc * 32, o);
-                    }
-                    tmem_wait_st();
-                }
-            }
-            // P half-row -> shared memory (column block hf), 128B-swizzled K-major
-#pragma unroll
-            for (int ch = 0; ch < HC / 8; ++ch) {
-                uint4 pk;
-                if (kF16) {
-                    __half2 h0 = __floats2half2_rn(s[ch * 8 + 0], s[ch * 8 + 1]);
-                    __half2 h1 = __floats2half2_rn(s[ch * 8 + 2], s[ch * 8 + 3]);
-                    __half2 h2 = __floats2half2_rn(s[ch * 8 + 4], s[ch * 8 + 5]);
-                    __half2 h3 = __floats2half2_rn(s[ch * 8 + 6], s[ch * 8 + 7]);
-                    pk.x = *reinterpret_cast<uint32_t *>(&h0);
-                    pk.y = *reinterpret_cast<uint32_t *>(&h1);
-                    pk.z = *reinterpret_cast<uint32_t *>(&h2);
-                    pk.w = *reinterpret_cast<uint32_t *>(&h3);
-                } else {
-                    __nv_bfloat162 h0 = __floats2bfloat162_rn(s[ch * 8 + 0], s[ch * 8 + 1]);
-                    __nv_bfloat162 h1 = __floats2bfloat162_rn(s[ch * 8 + 2], s[ch * 8 + 3]);
-                    __nv_bfloat162 h2 = __floats2bfloat162_rn(s[ch * 8 + 4], s[ch * 8 + 5]);
-                    __nv_bfloat162 h3 = __floats2bfloat162_rn(s[ch * 8 + 6], s[ch * 8 + 7]);
-                    pk.x = *reinterpret_cast<uint32_t *>(&h0);
-                    pk.y = *reinterpret_cast<uint32_t *>(&h1);
-                    pk.z = *reinterpret_cast<uint32_t *>(&h2);
-                    pk.w = *reinterpret_cast<uint32_t *>(&h3);
-                }
-                *reinterpret_cast<uint4 *>(prow + ((ch ^ (r & 7)) << 4)) = pk;
-            }
-            fence_proxy_async_smem();
+            l_run = l_run * alpha + (sum2.x + sum2.y);
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[x]);
         }
 
-        // epilogue: l = both halves' partial sums; O / l -> global
-        xch[(4 + hf) * BM + r] = l_part;  // its own buffer: the partner may still read a max slot
-        mbar_wait(o_done, (n_tiles - 1) & 1u, abort_flag, p.err);
+        // epilogue: O / l -> global
+        mbar_wait(&o_final[x], 0, abort_flag, p.err);
         __syncwarp();
-        named_bar_sync(2 + q4, 64);
-        const float l_row = l_part + xch[(4 + (hf ^ 1u)) * BM + r];
         tc_fence_after();
-        const float inv_l = 1.f / l_row;
+        const float inv_l = 1.f / l_run;
         const bool valid = t < p.S;
-        const size_t orow = ((size_t)(row_base + t) * p.H + h) * D + hf * HD;
+        const size_t orow = ((size_t)(row_base + t) * p.H + h) * D;
 #pragma unroll
-        for (int cc = 0; cc < HD / 32; ++cc) {
+        for (int cc = 0; cc < D / 32; ++cc) {
             float o[32];
-            tmem_ld32(tmem + lane_addr + C::O_COL + hf * HD + cc * 32, o);
+            tmem_ld32(o_col + cc * 32, o);
             tmem_wait_ld();
             if (valid) {
                 if (p.out_f32) {
@@ -460,21 +483,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 } else {
                     uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.out) + orow + cc * 32);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int k2 = 0; k2 < 4; ++k2) {
-                            const float a0 = o[8 * i + 2 * k2] * inv_l, a1 = o[8 * i + 2 * k2 + 1] * inv_l;
-                            if (kF16) {
-                                __half2 hv = __floats2half2_rn(a0, a1);
-                                w[k2] = *reinterpret_cast<uint32_t *>(&hv);
-                            } else {
-                                __nv_bfloat162 hv = __floats2bfloat162_rn(a0, a1);
-                                w[k2] = *reinterpret_cast<uint32_t *>(&hv);
-                            }
-                        }
-                        dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
+                    for (int i = 0; i < 4; ++i)
+                        dst[i] = make_uint4(pack2<kF16>(o[8 * i] * inv_l, o[8 * i + 1] * inv_l),
+                                            pack2<kF16>(o[8 * i + 2] * inv_l, o[8 * i + 3] * inv_l),
+                                            pack2<kF16>(o[8 * i + 4] * inv_l, o[8 * i + 5] * inv_l),
+                                            pack2<kF16>(o[8 * i + 6] * inv_l, o[8 * i + 7] * inv_l));
                 }
             }
         }
@@ -536,6 +549,21 @@ cudaError_t launch_t(const PrefillParams &p, unsigned grid, cudaStream_t stream)
 
 __device__ uint32_t g_prefill_err;
 
+// Device address of the prefill error word on the current device.
+uint32_t *prefill_err_word() {
+    static std::mutex mu;
+    static uint32_t *addr[64] = {nullptr};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void *ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_prefill_err) == cudaSuccess) addr[dev] = static_cast<uint32_t *>(ptr);
+    }
+    return addr[dev];
+}
+
 }  // namespace
 
 cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t stream) {
@@ -547,19 +575,18 @@ cudaError_t launch_prefill(const PrefillArgs &a, cudaStream_t stream) {
         !make_map(&p.tk, a.k, f16, a.head_dim, a.n_kv, rows) ||
         !make_map(&p.tv, a.v, f16, a.head_dim, a.n_kv, rows))
         return cudaErrorInvalidValue;
-    uint32_t *err = nullptr;
-    cudaGetSymbolAddress(reinterpret_cast<void **>(&err), g_prefill_err);
     p.out = a.out;
-    p.err = err;
+    p.err = prefill_err_word();
     p.S = a.seq_len;
     p.H = a.n_heads;
     p.Hkv = a.n_kv;
     p.n_seqs = a.n_seqs;
     p.n_mtiles = (a.seq_len + BM - 1) / BM;
+    p.n_pairs = (p.n_mtiles + 1) / 2;
     p.scale_log2 = (float)((double)a.scale * 1.4426950408889634);
     p.causal = a.causal ? 1 : 0;
     p.out_f32 = a.out_dtype == BML_F32 ? 1 : 0;
-    const uint64_t grid = (uint64_t)p.n_mtiles * a.n_seqs * a.n_heads;
+    const uint64_t grid = (uint64_t)p.n_pairs * a.n_seqs * a.n_heads;
     if (grid == 0 || grid > 0x7fffffffull) return cudaErrorInvalidValue;
     switch (a.head_dim) {
         case 64: return f16 ? launch_t<64, true>(p, (unsigned)grid, stream) : launch_t<64, false>(p, (unsigned)grid, stream);
