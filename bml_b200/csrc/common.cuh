@@ -63,11 +63,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test of the same condition.  On sm_100a it returns in a few
+// cycles when the phase has completed, where try_wait costs tens of cycles
+// even then -- which matters to a thread that feeds the tensor core, whose
+// instruction queue holds only about one MMA.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for phase `parity` of `bar` to complete.  `abort_flag` (shared) is
 // set once any wait of the CTA timed out; later waits then return at once.
 // Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
                                           volatile uint32_t *abort_flag, uint32_t *err) {
+    if (mbar_test_wait(bar, parity)) return true;
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer_ns();
     while (true) {

@@ -18,9 +18,10 @@
 //               swizzle, no multicast), completing on mbarriers.
 //   warp 1      allocates tensor memory; lane 0 issues every tcgen05.mma.
 //   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: thread r
-//               owns query row r (TMEM lane r).  It reads its S row in two
-//               passes over tensor memory (row max, then exponentials),
-//               writes P back over S as packed 16-bit pairs with tcgen05.st,
+//               owns query row r (TMEM lane r).  It loads its 128 scores
+//               from tensor memory at once, writes P back over S as packed
+//               16-bit pairs with tcgen05.st in two halves (P.V starts on the
+//               first half while the second is computed),
 //               and rescales O in TMEM only when its running max grew by
 //               more than 2^8 (the final O / l is exact for any fixed
 //               reference max).
@@ -46,6 +47,9 @@ constexpr int BN = 128;  // kv positions per tile
 constexpr int kThreads = 320;  // producer, MMA issuer, 4 + 4 softmax warps
 constexpr int kMaxStages = 4;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// The MMA warp tests the barriers of its next block of MMAs this many MMAs
+// before the end of the current block.
+constexpr int kGateLookahead = 1;
 
 template <int D>
 struct PCfg {
@@ -102,6 +106,17 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                      smem_u32(bar))
                  : "memory");
+}
+
+// true in exactly one lane of a converged warp
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, e;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]
@@ -164,6 +179,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
 }
 
 // 16 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *w) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
@@ -216,8 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     uint64_t *v_full = k_empty + kMaxStages;    // [stage]
     uint64_t *v_empty = v_full + kMaxStages;    // [stage]
     uint64_t *s_full = v_empty + kMaxStages;    // [chain]: S of the chain's current tile in TMEM
-    uint64_t *p_full = s_full + 2;              // [chain]: P of the chain's current tile in TMEM
-    uint64_t *o_final = p_full + 2;             // [chain]: last P.V of the chain done
+    uint64_t *p_full = s_full + 2;              // [chain][half]: P columns 32*half.. of the chain's tile in TMEM
+    uint64_t *o_final = p_full + 4;             // [chain]: last P.V of the chain done
     volatile uint32_t *misc = reinterpret_cast<volatile uint32_t *>(o_final + 2);  // [0] tmem base, [1] abort
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -249,7 +277,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
         for (int x = 0; x < 2; ++x) {
             mbar_init(&s_full[x], 1);
-            mbar_init(&p_full[x], 4);
+            mbar_init(&p_full[2 * x], 4);
+            mbar_init(&p_full[2 * x + 1], 4);
             mbar_init(&o_final[x], 1);
         }
         misc[1] = 0u;
@@ -301,58 +330,129 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t fmt = kF16 ? 0u : 1u;
-            constexpr uint32_t idesc_qk = make_idesc(fmt, BM, BN, 0);
-            constexpr uint32_t idesc_pv = make_idesc(fmt, BM, D, 1);
-            const uint32_t q_base = smem_u32(sQ), k_base = smem_u32(sK), v_base = smem_u32(sV);
-            mbar_wait(q_full, 0, abort_flag, p.err);
-            // S_x = Q_x K(j)^T.  The first chain to use K(j) waits for it;
-            // chain B, the last user, releases the stage.
-            auto issue_qk = [&](uint32_t x, uint32_t j) {
-                const uint32_t st = j % C::STAGES;
-                if (x == 0 || j >= nt0) {
-                    mbar_wait(&k_full[st], (j / C::STAGES) & 1u, abort_flag, p.err);
-                    tc_fence_after();
-                }
+        // The whole warp runs this loop converged and one elected lane issues
+        // each tcgen05 instruction.  The tensor core queues only about one MMA
+        // ahead, so every cycle spent between two MMAs beyond that is lost;
+        // measured on B200, barrier tests cost a single issuing thread (in a
+        // divergent branch) up to ~35 cycles per MMA while the softmax warps
+        // run beside it, and next to nothing for a converged warp.  Each block
+        // of MMAs also tests the barriers of the next block before its own last
+        // MMA and blocks on them only if they were not complete yet.
+        constexpr uint32_t fmt = kF16 ? 0u : 1u;
+        constexpr uint32_t idesc_qk = make_idesc(fmt, BM, BN, 0);
+        constexpr uint32_t idesc_pv = make_idesc(fmt, BM, D, 1);
+        // Base descriptors; an operand `bytes` further on is the base plus
+        // bytes >> 4 (the 14-bit start field never carries: shared memory
+        // addresses stay below 256 KB).
+        const uint64_t dq = smem_desc(smem_u32(sQ), 16, 1024);
+        const uint64_t dk = smem_desc(smem_u32(sK), 16, 1024);
+        const uint64_t dv = smem_desc(smem_u32(sV), BN * 128, 1024);
+        struct Gate {  // one or two barrier phases; b1 may be null
+            uint64_t *b0;
+            uint32_t p0;
+            uint64_t *b1;
+            uint32_t p1;
+        };
+        auto gate_test = [&](const Gate &g) {
+            bool ok = g.b0 == nullptr || mbar_test_wait(g.b0, g.p0);
+            if (g.b1) ok = ok & mbar_test_wait(g.b1, g.p1);
+            return ok;
+        };
+        auto gate_wait = [&](const Gate &g, bool ready) {
+            if (!ready) {
+                if (g.b0) mbar_wait(g.b0, g.p0, abort_flag, p.err);
+                if (g.b1) mbar_wait(g.b1, g.p1, abort_flag, p.err);
+            }
+            __syncwarp();
+            tc_fence_after();
+        };
+        // S_x = Q_x K(j)^T.  Chain B, the last user of K(j), releases the stage.
+        auto qk = [&](uint32_t x, uint32_t j, const Gate &next) {
+            const uint32_t st = j % C::STAGES;
+            const uint64_t a0 = dq + ((x * C::Q_BYTES) >> 4);
+            const uint64_t b0 = dk + ((st * C::TILE_BYTES) >> 4);
+            const uint32_t d = tmem + x * 128;
+            bool ready = true;
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = x * C::Q_BYTES + (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-                    const uint32_t koff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
-                    tc_mma_ss(tmem + x * 128, smem_desc(q_base + off, 16, 1024),
-                              smem_desc(k_base + st * C::TILE_BYTES + koff, 16, 1024), idesc_qk, kk > 0);
-                }
+            for (int kk = 0; kk < D / 16; ++kk) {
+                if (kk == D / 16 - kGateLookahead) ready = gate_test(next);
+                // k-step kk: 128B column block kk/4, 32 bytes per step inside it (BM == BN)
+                const uint32_t off = ((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4;
+                if (elect_one()) tc_mma_ss(d, a0 + off, b0 + off, idesc_qk, kk > 0);
+                __syncwarp();
+            }
+            if (elect_one()) {
                 tc_commit(&s_full[x]);
                 if (x == 1) tc_commit(&k_empty[st]);
-            };
-            // O_x += P_x V(j), P_x read from tensor memory (over S_x)
-            auto issue_pv = [&](uint32_t x, uint32_t j) {
-                const uint32_t st = j % C::STAGES;
-                mbar_wait(&p_full[x], j & 1u, abort_flag, p.err);
-                if (x == 0 || j >= nt0) mbar_wait(&v_full[st], (j / C::STAGES) & 1u, abort_flag, p.err);
-                tc_fence_after();
+            }
+            __syncwarp();
+            return ready;
+        };
+        // O_x += P_x V(j) over kv rows 64h..64h+63, P_x read from tensor
+        // memory (over S_x).  The softmax releases P in these two halves,
+        // so the first half of P.V overlaps the second half of its work.
+        auto pv = [&](uint32_t x, uint32_t j, int h, const Gate &next) {
+            const uint32_t st = j % C::STAGES;
+            const uint64_t b0 = dv + ((st * C::TILE_BYTES) >> 4);
+            const uint32_t d = tmem + C::O_COL0 + x * D, a = tmem + x * 128;
+            bool ready = true;
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint32_t voff = kk * 16 * 128;  // 16 kv rows of 128 B
-                    tc_mma_ts(tmem + C::O_COL0 + x * D, tmem + x * 128 + kk * 8,
-                              smem_desc(v_base + st * C::TILE_BYTES + voff, BN * 128, 1024), idesc_pv,
-                              (j > 0 || kk > 0) ? 1u : 0u);
-                }
+            for (int k4 = 0; k4 < BN / 32; ++k4) {
+                const int kk = h * (BN / 32) + k4;  // 16 kv rows of 128 B per step
+                if (k4 == BN / 32 - kGateLookahead) ready = gate_test(next);
+                if (elect_one())
+                    tc_mma_ts(d, a + kk * 8, b0 + ((kk * 16 * 128) >> 4), idesc_pv, (kk > 0 || j > 0) ? 1u : 0u);
+                __syncwarp();
+            }
+            if (h == 1 && elect_one()) {
                 if (x == 1) tc_commit(&v_empty[st]);
                 if (j + 1 == (x ? nt1 : nt0)) tc_commit(&o_final[x]);
-            };
-            issue_qk(0, 0);
-            issue_qk(1, 0);
-            for (uint32_t j = 0; j < nt1; ++j) {
-                if (j < nt0) {
-                    issue_pv(0, j);
-                    if (j + 1 < nt0) issue_qk(0, j + 1);
+            }
+            __syncwarp();
+            return ready;
+        };
+        // gate of the first P.V block of iteration j: chain A's while it runs
+        // (chain A is then the first user of V(j)), else chain B's
+        auto gate_pv0 = [&](uint32_t j) {
+            const uint32_t st = j % C::STAGES, ph = (j / C::STAGES) & 1u;
+            return Gate{&p_full[j < nt0 ? 0 : 2], j & 1u, &v_full[st], ph};
+        };
+        const Gate none = {nullptr, 0u, nullptr, 0u};
+
+        gate_wait(Gate{q_full, 0u, &k_full[0], 0u}, false);
+        qk(0, 0, none);
+        gate_wait(gate_pv0(0), qk(1, 0, gate_pv0(0)));
+        for (uint32_t j = 0; j < nt1; ++j) {
+            const uint32_t jp = j & 1u;
+            const uint32_t st1 = (j + 1) % C::STAGES, ph1 = ((j + 1) / C::STAGES) & 1u;
+            if (j < nt0) {
+                {
+                    const Gate g = {&p_full[1], jp, nullptr, 0u};
+                    gate_wait(g, pv(0, j, 0, g));
                 }
-                issue_pv(1, j);
-                if (j + 1 < nt1) issue_qk(1, j + 1);
+                if (j + 1 < nt0) {
+                    const Gate g2 = {&k_full[st1], ph1, nullptr, 0u};
+                    gate_wait(g2, pv(0, j, 1, g2));
+                    const Gate g3 = {&p_full[2], jp, nullptr, 0u};
+                    gate_wait(g3, qk(0, j + 1, g3));
+                } else {
+                    const Gate g2 = {&p_full[2], jp, nullptr, 0u};
+                    gate_wait(g2, pv(0, j, 1, g2));
+                }
+            }
+            {
+                const Gate g = {&p_full[3], jp, nullptr, 0u};
+                gate_wait(g, pv(1, j, 0, g));
+            }
+            if (j + 1 < nt1) {
+                const Gate g5 = (j + 1 >= nt0) ? Gate{&k_full[st1], ph1, nullptr, 0u} : none;
+                gate_wait(g5, pv(1, j, 1, g5));
+                const Gate g6 = gate_pv0(j + 1);
+                gate_wait(g6, qk(1, j + 1, g6));
+            } else {
+                pv(1, j, 1, none);
             }
         }
-        __syncwarp();
     } else {
         // ------------------------------------------------------------- softmax
         const uint32_t x = (uint32_t)(warp - 2) >> 2;  // chain: 0 = tile A (warps 2-5), 1 = tile B (6-9)
@@ -374,30 +474,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             const uint32_t kv0 = j * BN;
             const bool mask_tile = kv0 + BN - 1 > lim;
 
-            // pass 1: row max, 8 chains of three-input max per 64 columns
-            float mh = -INFINITY;
+            // all 128 scores of the row in one round trip
+            float sv[BN];
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                float s[64];
-                tmem_ld32(s_col + half * 64, s);
-                tmem_ld32(s_col + half * 64 + 32, s + 32);
-                tmem_wait_ld();
-                if (mask_tile) {
+            for (int cc = 0; cc < BN / 32; ++cc) tmem_ld32(s_col + cc * 32, sv + cc * 32);
+            tmem_wait_ld();
+            if (mask_tile) {
 #pragma unroll
-                    for (int i = 0; i < 64; ++i)
-                        if (kv0 + half * 64 + i > lim) s[i] = -INFINITY;
-                }
-                float mx8[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    float a = fmax3(s[k], s[k + 8], s[k + 16]);
-                    a = fmax3(a, s[k + 24], s[k + 32]);
-                    a = fmax3(a, s[k + 40], s[k + 48]);
-                    mx8[k] = fmaxf(a, s[k + 56]);
-                }
-                mh = fmax3(mh, fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]));
-                mh = fmax3(mh, mx8[6], mx8[7]);
+                for (int i = 0; i < BN; ++i)
+                    if (kv0 + i > lim) sv[i] = -INFINITY;
             }
+            // row max: 8 independent chains of three-input max
+            float mx8[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                float a = fmax3(sv[k], sv[k + 8], sv[k + 16]);
+#pragma unroll
+                for (int i = 24; i < BN - 8; i += 16) a = fmax3(a, sv[k + i], sv[k + i + 8]);  // up to k+112
+                mx8[k] = fmaxf(a, sv[k + BN - 8]);                                              // k+120
+            }
+            const float mh = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
             const float m_tile = mh * c;
             float m_new = m_run;
             if (m_run == -INFINITY || m_tile > m_run + kRescaleThreshold) m_new = fmaxf(m_run, m_tile);
@@ -406,59 +502,53 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             const bool rescale = (j > 0) && (m_new != m_run);
             m_run = m_new;
 
-            // O rescale (rare).  PV_x(j-1) has finished: S_x(j) was issued
-            // after it and its commit covers every earlier MMA.
-            if (__any_sync(0xffffffffu, rescale)) {
-                const float a = rescale ? alpha : 1.f;
-#pragma unroll
-                for (int cc = 0; cc < D / 32; ++cc) {
-                    float o[32];
-                    tmem_ld32(o_col + cc * 32, o);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] *= a;
-                    tmem_st32(o_col + cc * 32, o);
-                }
-            }
-
-            // pass 2: p = 2^(s*c - m), 32 columns at a time, written back as
-            // packed 16-bit pairs over columns already read: P chunk q goes to
-            // columns 16q..16q+15, S chunk q came from 32q..32q+31.  One pair
-            // in four of the exponentials runs on the FMA/ALU pipes.
+            // p = 2^(s*c - m), written as packed 16-bit pairs into columns
+            // 0..63 of S_x (kv 2i, 2i+1 -> column i) and released to the MMA
+            // warp in two halves.  All exponentials run on the SFU: measured on
+            // B200, moving a share of them to a polynomial on the FMA pipe
+            // (exp2_poly2) costs more issue slots than it frees SFU time here.
             const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
             float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                               make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int qc = 0; qc < BN / 32; ++qc) {
-                float s[32];
-                tmem_ld32(s_col + qc * 32, s);
-                tmem_wait_ld();
-                if (mask_tile) {
+            for (int hv = 0; hv < 2; ++hv) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (kv0 + qc * 32 + i > lim) s[i] = -INFINITY;
-                }
-                uint32_t w[16];
+                for (int q2 = 0; q2 < 2; ++q2) {
+                    const int qc = hv * 2 + q2;
+                    uint32_t w[16];
 #pragma unroll
-                for (int i = 0; i < 32; i += 2) {
-                    float2 e = __ffma2_rn(make_float2(s[i], s[i + 1]), c2, nm2);
-                    if (((i >> 1) & 3) == 3) {
-                        e = exp2_poly2(e);
-                    } else {
+                    for (int i = 0; i < 32; i += 2) {
+                        float2 e = __ffma2_rn(make_float2(sv[qc * 32 + i], sv[qc * 32 + i + 1]), c2, nm2);
                         e.x = fast_exp2(e.x);
                         e.y = fast_exp2(e.y);
+                        sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], e);
+                        w[i >> 1] = pack2<kF16>(e.x, e.y);
                     }
-                    sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], e);
-                    w[i >> 1] = pack2<kF16>(e.x, e.y);
+                    tmem_st16(s_col + qc * 16, w);
                 }
-                tmem_st16(s_col + qc * 16, w);
+                if (hv == 0 && __any_sync(0xffffffffu, rescale)) {
+                    // O rescale (rare), before P.V(j) accumulates into O_x and
+                    // after half of the scores are dead.  PV_x(j-1) has
+                    // finished: S_x(j) was issued after it and its commit covers
+                    // every earlier MMA.
+                    const float a = rescale ? alpha : 1.f;
+#pragma unroll
+                    for (int cc = 0; cc < D / 32; ++cc) {
+                        float o[32];
+                        tmem_ld32(o_col + cc * 32, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] *= a;
+                        tmem_st32(o_col + cc * 32, o);
+                    }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[2 * x + hv]);
             }
             const float2 sum2 = __fadd2_rn(__fadd2_rn(sum4[0], sum4[1]), __fadd2_rn(sum4[2], sum4[3]));
             l_run = l_run * alpha + (sum2.x + sum2.y);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[x]);
         }
 
         // epilogue: O / l -> global
