@@ -59,6 +59,17 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
+def decode_kernel_name(kv_dtype: torch.dtype, head_dim: int, n_kv: int, group: int) -> str:
+    """Kernel that bml_attn_decode_batched launches for a shape: the
+    warp-MMA kernel for 16-bit caches with 512..2048-byte position rows, the
+    CUDA-core kernel otherwise (mirrors decode_mma_supported in
+    bml_b200/csrc/decode_mma.cu)."""
+    row = n_kv * head_dim * 2
+    mma = (kv_dtype in (torch.float16, torch.bfloat16) and head_dim in (64, 128) and group in (1, 2, 4, 8)
+           and n_kv in (1, 2, 4, 8) and 512 <= row <= 2048)
+    return "decode_mma_kernel" if mma else "decode_kernel"
+
+
 def profile_traffic(name: str):
     """traffic_bytes_per_launch recorded from an ncu capture in profiles/."""
     path = os.path.join(ROOT, "profiles", name)
@@ -432,7 +443,8 @@ def run_b200(args):
         "ms_per_step": round(ms / args.steps, 5), "scaling": scaling, "dtype": dtype, "config": cfg,
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(ach / hbm, 4), "traffic": profile_traffic(f"decode_{wl}.txt"),
-                     "kernel": "decode_kernel", "kernel_ms": round(kms, 5),
+                     "kernel": decode_kernel_name(batch.dtype, batch.head_dim, batch.n_kv, H // batch.n_kv),
+                     "kernel_ms": round(kms, 5),
                      "algorithmic_bytes_per_launch": step_bytes},
         "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps,
     })
@@ -524,7 +536,8 @@ def run_longctx(args, dist, peaks, res):
                            "l2": "256 MiB of KV per step on 1 GPU"},
                 "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                              "frac": round(ach / hbm, 4), "traffic": profile_traffic("decode_longctx.txt"),
-                             "kernel": "decode_kernel", "kernel_ms": round(kms, 5)},
+                             "kernel": decode_kernel_name(torch.bfloat16, d, Hkv, H // Hkv),
+                             "kernel_ms": round(kms, 5)},
                 "clocks": clocks, "gpu_launches": args.steps * (1 if dist.world == 1 else 2)})
     if dist.world == 1 and not args.no_cpu:
         v, thr, desc = cpu_decode_sample("longctx", args.cpu_budget)

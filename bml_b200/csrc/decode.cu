@@ -41,22 +41,25 @@ constexpr int kSmemBudget = 227 * 1024;
 
 // Kernel geometry.  NW warps; warp w serves kv head w % n_kv, the w-th
 // "head split" (GW of the G q heads sharing that kv head) and a row phase.
-template <typename KT, int D, int G, int GW, int NW>
+// LPR lanes share one KV row (8 or 16), so a warp step covers RPS = 32/LPR
+// rows.
+template <typename KT, int D, int G, int GW, int NW, int LPR>
 struct Cfg {
     static constexpr int THREADS = NW * 32;
     static constexpr int HS = G / GW;       // head splits per kv head
+    static constexpr int RPS = 32 / LPR;    // rows per warp step
     static constexpr int ES = sizeof(KT);
     static constexpr int HEAD_BYTES = D * ES;
     static constexpr int CHUNKS = HEAD_BYTES / 16;
-    static constexpr int CPL = CHUNKS / 8;  // 16-byte chunks per lane
+    static constexpr int CPL = CHUNKS / LPR;  // 16-byte chunks per lane
     static constexpr int EPC = 16 / ES;     // elements per chunk
     static constexpr int E = CPL * EPC;     // elements per lane
     static constexpr int E2 = E / 2;        // float2 pairs per lane
     static constexpr int STAGE_K = 32768;   // K bytes per stage; V the same
     // rows per tile T = STAGE_K / (n_kv*HEAD_BYTES); rows per warp = T / nph
-    // with nph = NW / (n_kv*HS); 4 rows per warp step.
-    static constexpr int STEPS = STAGE_K * HS / (HEAD_BYTES * NW * 4);
-    static constexpr int WSCR = 4 * GW /*alpha*/ + 4 * STEPS * GW /*p*/ + 4 * GW * 2 /*ml*/;
+    // with nph = NW / (n_kv*HS); RPS rows per warp step.
+    static constexpr int STEPS = STAGE_K * HS / (HEAD_BYTES * NW * RPS);
+    static constexpr int WSCR = RPS * GW /*alpha*/ + RPS * STEPS * GW /*p*/ + RPS * GW * 2 /*ml*/;
     static constexpr int EXTRA = 2 * 8 * 8 /*barriers*/ + 16 +
                                  4 * (NW * WSCR + NW * GW * D + NW * GW * 2);
     static constexpr int STAGES_FIT = (kSmemBudget - EXTRA) / (2 * STAGE_K);
@@ -64,7 +67,9 @@ struct Cfg {
     static constexpr int BAR_OFF = STAGES * 2 * STAGE_K;
     static constexpr int SMEM = BAR_OFF + EXTRA;
     static_assert(G % GW == 0, "head split");
-    static_assert(CHUNKS % 8 == 0, "head row must be a multiple of 128 bytes");
+    static_assert(LPR == 8 || LPR == 16, "lanes per row");
+    static_assert(GW <= LPR, "one owner lane per q head");
+    static_assert(CHUNKS % LPR == 0, "head row must be a multiple of LPR 16-byte chunks");
     static_assert(STEPS >= 1, "stage too small");
     static_assert(STAGES >= 2, "shared memory budget");
 };
@@ -79,16 +84,17 @@ __device__ __forceinline__ uint32_t tile_end_of(const DecodeParams &p, uint32_t 
     return s + 1 < p.n_seqs ? p.seqs[s + 1].tile_begin : p.total_tiles;
 }
 
-// Butterfly reduction of G per-lane partial sums across the 8 lanes of a
-// lane group that also transposes: on return, lane j (j = lane & 7) holds
-// the full sum of value index j*G/8.
-template <int G>
+// Butterfly reduction of G per-lane partial sums across the LPR lanes of a
+// lane group that also transposes: on return, lane j (j = lane % LPR) holds
+// the full sum of value index j*G/LPR.
+template <int G, int LPR>
 __device__ __forceinline__ float transpose_reduce(float (&v)[G], int j) {
     constexpr unsigned FULL = 0xffffffffu;
+    constexpr int LEVELS = LPR == 16 ? 4 : 3;
     int n = G;
 #pragma unroll
-    for (int lvl = 0; lvl < 3; ++lvl) {
-        const int mask = 4 >> lvl;
+    for (int lvl = 0; lvl < LEVELS; ++lvl) {
+        const int mask = (LPR / 2) >> lvl;
         const bool upper = (j & mask) != 0;
         if (n >= 2) {
             const int half = n / 2;
@@ -108,10 +114,10 @@ __device__ __forceinline__ float transpose_reduce(float (&v)[G], int j) {
     return v[0];
 }
 
-template <typename KT, int D, int G, int GW, int NW>
+template <typename KT, int D, int G, int GW, int NW, int LPR>
 __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
-    using C = Cfg<KT, D, G, GW, NW>;
-    constexpr int STEPS = C::STEPS, E2 = C::E2, CPL = C::CPL, EPC = C::EPC, HS = C::HS;
+    using C = Cfg<KT, D, G, GW, NW, LPR>;
+    constexpr int STEPS = C::STEPS, E2 = C::E2, CPL = C::CPL, EPC = C::EPC, HS = C::HS, RPS = C::RPS;
     constexpr int HEAD_BYTES = C::HEAD_BYTES, STAGE_K = C::STAGE_K, NST = C::STAGES;
     constexpr int WSCR = C::WSCR, THREADS = C::THREADS;
     constexpr float NEG_INF = -INFINITY;
@@ -119,8 +125,9 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t *stages = smem;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
-    uint64_t *empty = full + 8;
-    volatile uint32_t *flags = reinterpret_cast<volatile uint32_t *>(empty + 8);
+    // per stage: warps done with it; [8], [9]: refill cursor (sequence, tile)
+    volatile uint32_t *cnt = reinterpret_cast<volatile uint32_t *>(full + 8);
+    volatile uint32_t *flags = reinterpret_cast<volatile uint32_t *>(full + 16);
     float *wscr = reinterpret_cast<float *>(smem + C::BAR_OFF + 2 * 8 * 8 + 16);
     float *wsum = wscr + NW * WSCR;  // [NW warps][GW][D]
     float *wml = wsum + NW * GW * D;  // [NW warps][GW][2]
@@ -133,7 +140,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
     if (threadIdx.x == 0) {
         for (int i = 0; i < NST; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], NW);
+            cnt[i] = 0u;
         }
         flags[0] = 0u;
         flags[1] = 0u;
@@ -142,30 +149,33 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
     __syncthreads();
     if (t_begin >= t_end) return;
 
-    // Thread 0 doubles as the producer: it fills the ring ahead of the
-    // consumers and refills a stage as soon as every warp released it.
-    // (A separate producer warp would unbalance the 4 sub-partitions of the
-    // SM, whose register files each serve a quarter of the warps.)
-    uint64_t pol = 0;
-    uint32_t ps = 0, pt = t_begin;  // producer cursor: sequence, tile
+    // Thread 0 fills the ring; afterwards the last warp to finish with a
+    // stage refills it (an shared-memory counter per stage), so no warp waits
+    // for the others before it starts its next tile.  Refills happen in tile
+    // order, so the cursor (sequence, tile) kept in shared memory advances
+    // monotonically; each warp's acquire-release increment of every tile's
+    // counter orders one refiller's cursor update before the next one's read.
     auto issue = [&](uint32_t it) {
+        uint32_t ps = cnt[8], pt = cnt[9];
         while (pt >= tile_end_of(p, ps)) ++ps;
         const uint32_t stage = it % NST;
         const uint32_t row0 = (pt - p.seqs[ps].tile_begin) * T;
         const uint32_t rows = min(T, p.seqs[ps].len - row0);
         const uint32_t bytes = rows * p.row_bytes;
         uint8_t *sk = stages + stage * 2 * STAGE_K;
+        const uint64_t pol = l2_policy_evict_first();
         mbar_arrive_expect_tx(&full[stage], 2 * bytes);
         const uint8_t *gk = static_cast<const uint8_t *>(p.seqs[ps].k) + (size_t)row0 * p.row_bytes;
         const uint8_t *gv = static_cast<const uint8_t *>(p.seqs[ps].v) + (size_t)row0 * p.row_bytes;
         bulk_g2s_stream(sk, gk, bytes, &full[stage], pol);
         bulk_g2s_stream(sk + STAGE_K, gv, bytes, &full[stage], pol);
-        ++pt;
+        cnt[8] = ps;
+        cnt[9] = pt + 1;
     };
     const uint32_t n_tiles = t_end - t_begin;
     if (threadIdx.x == 0) {
-        pol = l2_policy_evict_first();
-        ps = seq_of_tile(p, t_begin);
+        cnt[8] = seq_of_tile(p, t_begin);
+        cnt[9] = t_begin;
         for (uint32_t it = 0; it < n_tiles && it < (uint32_t)NST; ++it) issue(it);
     }
 
@@ -174,13 +184,13 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
     const int h = warp % n_kv;
     const int hs = (warp / n_kv) % HS;
     const int ph = warp / (n_kv * HS);
-    const int grp = lane >> 3, j = lane & 7;
-    const int own = (j * GW) >> 3;
-    const bool owner_lane = (j & ((8 / GW) - 1)) == 0;
+    const int grp = lane / LPR, j = lane % LPR;
+    const int own = (j * GW) / LPR;
+    const bool owner_lane = (j % (LPR / GW)) == 0;
     float *scr = wscr + warp * WSCR;
-    float *s_alpha = scr;                // [4][GW]
-    float *s_p = scr + 4 * GW;           // [4][STEPS][GW]
-    float *s_ml = s_p + 4 * STEPS * GW;  // [4][GW][2]
+    float *s_alpha = scr;                  // [RPS][GW]
+    float *s_p = scr + RPS * GW;           // [RPS][STEPS][GW]
+    float *s_ml = s_p + RPS * STEPS * GW;  // [RPS][GW][2]
 
     float2 q2[GW][E2], acc[GW][E2];
     float m_own = NEG_INF, l_own = 0.f;
@@ -192,7 +202,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
         for (int hh = 0; hh < GW; ++hh) {
 #pragma unroll
             for (int c = 0; c < CPL; ++c) {
-                const float4 *src = reinterpret_cast<const float4 *>(qs + hh * D + (j + 8 * c) * EPC);
+                const float4 *src = reinterpret_cast<const float4 *>(qs + hh * D + (j + LPR * c) * EPC);
 #pragma unroll
                 for (int f = 0; f < EPC / 4; ++f) {
                     const float4 v = __ldg(src + f);
@@ -223,7 +233,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
         float sc[STEPS];
 #pragma unroll
         for (int st = 0; st < STEPS; ++st) {
-            const uint32_t r = (uint32_t)((st * nph + ph) * 4 + grp);
+            const uint32_t r = (uint32_t)((st * nph + ph) * RPS + grp);
             float2 part2[GW];
 #pragma unroll
             for (int hh = 0; hh < GW; ++hh) part2[hh] = make_float2(0.f, 0.f);
@@ -231,7 +241,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
                 const uint8_t *rowp = sk + (size_t)r * p.row_bytes;
 #pragma unroll
                 for (int c = 0; c < CPL; ++c) {
-                    const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (j + 8 * c) * 16);
+                    const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (j + LPR * c) * 16);
                     float2 kf[EPC / 2];
                     Elem<KT>::widen2(raw, kf);
 #pragma unroll
@@ -244,7 +254,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
             float part[GW];
 #pragma unroll
             for (int hh = 0; hh < GW; ++hh) part[hh] = part2[hh].x + part2[hh].y;
-            const float tot = transpose_reduce<GW>(part, j);
+            const float tot = transpose_reduce<GW, LPR>(part, j);
             sc[st] = (r < rows) ? tot : NEG_INF;
         }
         float mt = sc[0];
@@ -288,7 +298,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
         // pass 2: P.V
 #pragma unroll
         for (int st = 0; st < STEPS; ++st) {
-            const uint32_t r = (uint32_t)((st * nph + ph) * 4 + grp);
+            const uint32_t r = (uint32_t)((st * nph + ph) * RPS + grp);
             if (r < rows) {
                 float2 pp[GW];
 #pragma unroll
@@ -299,7 +309,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
                 const uint8_t *rowp = sv + (size_t)r * p.row_bytes;
 #pragma unroll
                 for (int c = 0; c < CPL; ++c) {
-                    const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (j + 8 * c) * 16);
+                    const uint4 raw = *reinterpret_cast<const uint4 *>(rowp + (j + LPR * c) * 16);
                     float2 vf[EPC / 2];
                     Elem<KT>::widen2(raw, vf);
 #pragma unroll
@@ -310,11 +320,20 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
-        if (threadIdx.x == 0 && it + NST < n_tiles) {
-            mbar_wait(&empty[stage], (it / NST) & 1u, flags, p.err);
-            issue(it + NST);
+        __syncwarp();  // the warp's shared-memory reads of the stage precede lane 0's release
+        if (lane == 0) {
+            uint32_t old;
+            asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                         : "=r"(old)
+                         : "r"(smem_u32((const void *)&cnt[stage]))
+                         : "memory");
+            if (old == (uint32_t)NW - 1) {
+                cnt[stage] = 0u;
+                if (it + NST < n_tiles) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    issue(it + NST);
+                }
+            }
         }
 
         const bool last_of_cta = (t + 1 == t_end);
@@ -330,16 +349,18 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
         float Mh[GW], Lh[GW];
 #pragma unroll
         for (int hh = 0; hh < GW; ++hh) {
-            float mg[4], lg[4];
+            float mg[RPS], lg[RPS];
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
+            for (int g = 0; g < RPS; ++g) {
                 mg[g] = s_ml[(g * GW + hh) * 2 + 0];
                 lg[g] = s_ml[(g * GW + hh) * 2 + 1];
             }
-            const float M = fmaxf(fmaxf(mg[0], mg[1]), fmaxf(mg[2], mg[3]));
+            float M = mg[0];
+#pragma unroll
+            for (int g = 1; g < RPS; ++g) M = fmaxf(M, mg[g]);
             float L = 0.f, mine = 0.f;
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
+            for (int g = 0; g < RPS; ++g) {
                 const float f = (mg[g] == NEG_INF) ? 0.f : fast_exp2(mg[g] - M);
                 L += lg[g] * f;
                 if (g == grp) mine = f;
@@ -354,10 +375,11 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
         for (int hh = 0; hh < GW; ++hh)
 #pragma unroll
             for (int e = 0; e < E2; ++e) {
-                acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 8);
-                acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 8);
-                acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 16);
-                acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 16);
+#pragma unroll
+                for (int m = LPR; m < 32; m <<= 1) {
+                    acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, m);
+                    acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, m);
+                }
             }
         float *ws = wsum + warp * GW * D;
         if (grp == 0) {
@@ -367,7 +389,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
                 for (int c = 0; c < CPL; ++c)
 #pragma unroll
                     for (int e = 0; e < EPC / 2; ++e)
-                        *reinterpret_cast<float2 *>(ws + hh * D + (j + 8 * c) * EPC + 2 * e) = acc[hh][c * (EPC / 2) + e];
+                        *reinterpret_cast<float2 *>(ws + hh * D + (j + LPR * c) * EPC + 2 * e) = acc[hh][c * (EPC / 2) + e];
         }
         if (lane == 0) {
 #pragma unroll
@@ -463,33 +485,41 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
     }
 }
 
-template <typename KT, int D, int G, int GW, int NW>
+template <typename KT, int D, int G, int GW, int NW, int LPR>
 cudaError_t launch_one(const DecodeParams &p, int grid, cudaStream_t stream) {
-    using C = Cfg<KT, D, G, GW, NW>;
+    using C = Cfg<KT, D, G, GW, NW, LPR>;
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KT, D, G, GW, NW>,
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<KT, D, G, GW, NW, LPR>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    decode_kernel<KT, D, G, GW, NW><<<grid, C::THREADS, C::SMEM, stream>>>(p);
+    decode_kernel<KT, D, G, GW, NW, LPR><<<grid, C::THREADS, C::SMEM, stream>>>(p);
     return cudaGetLastError();
 }
 
-// Warp layout per (dtype, head_dim, group): GW q heads per warp so that q and
-// the accumulators fit in the register budget of 16 warps (<= 128 registers
-// a thread); shapes whose kv heads times head splits exceed 16 warps use 8
-// warps with all G heads in a warp.
+// Warp layout per (dtype, head_dim, group).  A KV row is spread over LPR =
+// 16 lanes when it has at least 16 chunks of 16 bytes (d=128 16-bit, f32),
+// else over 8; each warp carries GW q heads so that q and the accumulators
+// fit in the register budget of 16 warps (<= 128 registers a thread).  With
+// 16 lanes a row, a group of up to 4 q heads fits in one warp, so every K/V
+// element is read from shared memory and widened once.  Shapes whose kv
+// heads times head splits exceed 16 warps use 8 warps with all G heads in a
+// warp.
 template <typename KT, int D, int G>
 cudaError_t launch_shape(const DecodeParams &p, int grid, cudaStream_t stream) {
-    constexpr int E2 = (D * (int)sizeof(KT) / 128) * (16 / (int)sizeof(KT)) / 2;
+    constexpr int CHUNKS = D * (int)sizeof(KT) / 16;
+    constexpr int LPR = CHUNKS >= 16 ? 16 : 8;
+    constexpr int E2 = (CHUNKS / LPR) * (16 / (int)sizeof(KT)) / 2;
     constexpr int GW = G <= 1 ? 1 : (G * E2 <= 16 ? G : (16 / E2 >= 1 ? 16 / E2 : 1));
     constexpr int HS = G / GW;
-    if ((int)p.n_kv * HS <= 16) return launch_one<KT, D, G, GW, 16>(p, grid, stream);
-    return launch_one<KT, D, G, G, 8>(p, grid, stream);
+    if ((int)p.n_kv * HS <= 16) return launch_one<KT, D, G, GW, 16, LPR>(p, grid, stream);
+    constexpr int E2_8 = (CHUNKS / 8) * (16 / (int)sizeof(KT)) / 2;
+    static_assert(E2_8 >= 1, "row too short");
+    return launch_one<KT, D, G, G, 8, 8>(p, grid, stream);
 }
 
 template <typename KT, int D>
@@ -616,7 +646,8 @@ cudaError_t launch_slot_merge(const DecodeParams &p, uint32_t head_dim, cudaStre
 }
 
 uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv) {
-    // STEPS * 4 rows * (8 / n_kv) warps per head; equal to STAGE_K / row_bytes
+    // STAGE_K bytes of K per tile: STEPS * RPS rows for each of the row
+    // phases of a kv head
     const uint32_t row_bytes = n_kv * head_dim * (uint32_t)dtype_size(dt);
     return 32768u / row_bytes;
 }
@@ -661,6 +692,10 @@ bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_
 
 cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                           int grid, cudaStream_t stream) {
+    // 16-bit caches of the common shapes take the tensor-core kernel
+    // (decode_mma.cu); everything else the CUDA-core kernel below.
+    if (decode_mma_supported(dt, head_dim, p.n_kv, group))
+        return launch_decode_mma(p, dt, head_dim, group, grid, stream);
     switch (dt) {
         case BML_F32: return launch_d<float>(p, head_dim, group, grid, stream);
         case BML_F16: return launch_d<__half>(p, head_dim, group, grid, stream);

@@ -67,6 +67,13 @@ uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv);
 cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim,
                           uint32_t group, int grid, cudaStream_t stream);
 
+// Tensor-core (mma.sync m16n8k16) variant for 16-bit caches, same
+// parameters and schedule (decode_mma.cu).  launch_decode dispatches to it
+// for the shapes decode_mma_supported accepts.
+bool decode_mma_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
+cudaError_t launch_decode_mma(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
+                              int grid, cudaStream_t stream);
+
 // Merge of split-K slots for sequences spread over more CTAs than the
 // in-kernel merge handles well; one CTA per (sequence, head) row.
 cudaError_t launch_slot_merge(const DecodeParams &p, uint32_t head_dim, cudaStream_t stream);
