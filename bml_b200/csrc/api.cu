@@ -19,7 +19,6 @@
 
 #include "../../include/bml_attn.h"
 #include "decode.cuh"
-#include "decode_tc.cuh"
 #include "kv_ops.cuh"
 #include "prefill.cuh"
 
@@ -314,64 +313,6 @@ bml_status check_decode_shape(uint32_t n_heads, uint32_t n_kv, uint32_t head_dim
     return BML_OK;
 }
 
-// The tensor-core decode kernel (decode_tc.cu) stays disabled until its
-// d=128 fault is understood; every decode runs on decode.cu meanwhile.
-constexpr bool kUseTensorCoreDecode = false;
-
-// Tensor-core decode (16-bit KV): units are (sequence, kv head), 128-position
-// tiles, one CTA per SM over the flattened tile list.
-bml_status decode_tc_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv,
-                          uint32_t head_dim, bml_dtype dt, float sc, const float *q, float *out, float *pm, float *pl,
-                          float *po, const bml::DecodeWorkspace &ws, int sms, void *stream, int mode, const char *fn) {
-    static thread_local bml::TcParams p;
-    const uint32_t G = n_heads / n_kv;
-    for (uint32_t base = 0; base < n_seqs; base += bml::kMaxSeqsPerLaunch) {
-        const uint32_t ns = std::min<uint32_t>(n_seqs - base, bml::kMaxSeqsPerLaunch);
-        memset(&p, 0, offsetof(bml::TcParams, seqs));
-        uint64_t total = 0;
-        for (uint32_t s = 0; s < ns; ++s) total += (uint64_t)n_kv * ((seqs[base + s].len + 127) / 128);
-        if (total > 0x7fffffffull) return fail(BML_E_INVALID, "%s: batch too large", fn);
-        const uint32_t tpc = (uint32_t)((total + sms - 1) / sms);
-        const int grid = (int)((total + tpc - 1) / tpc);
-        uint32_t tile = 0;
-        uint64_t slot = 0;
-        for (uint32_t s = 0; s < ns; ++s) {
-            const bml_seq_desc &d = seqs[base + s];
-            bml::TcSeq &e = p.seqs[s];
-            e.k = d.k_dev;
-            e.v = d.v_dev;
-            e.len = d.len;
-            e.tiles = (d.len + 127) / 128;
-            e.tile_begin = tile;
-            e.slots_per_unit = (e.tiles + tpc - 1) / tpc + 1;
-            e.slot_base = (uint32_t)slot;
-            tile += n_kv * e.tiles;
-            slot += (uint64_t)n_kv * e.slots_per_unit;
-        }
-        // slots hold G rows each; the workspace holds max_slots * n_heads rows
-        if (slot * G > (uint64_t)ws.max_slots * n_heads) return fail(BML_E_INVALID, "%s: internal slot overflow", fn);
-        p.q = q + (size_t)base * n_heads * head_dim;
-        p.out = out ? out + (size_t)base * n_heads * head_dim : nullptr;
-        p.part_m = pm ? pm + (size_t)base * n_heads : nullptr;
-        p.part_l = pl ? pl + (size_t)base * n_heads : nullptr;
-        p.part_o = po ? po + (size_t)base * n_heads * head_dim : nullptr;
-        p.slot_ml = ws.slot_ml;
-        p.slot_o = ws.slot_o;
-        p.counters = ws.counters;
-        p.err = ws.err;
-        p.n_seqs = ns;
-        p.n_heads = n_heads;
-        p.n_kv = n_kv;
-        p.total_tiles = (uint32_t)total;
-        p.tiles_per_cta = tpc;
-        p.row_bytes = n_kv * head_dim * 2;
-        p.qscale = (float)((double)sc * 1.4426950408889634);
-        p.mode = mode;
-        CUDA_TRY(bml::launch_decode_tc(p, dt, head_dim, G, grid, static_cast<cudaStream_t>(stream)), fn);
-    }
-    return ok();
-}
-
 // Shared body of bml_attn_decode_batched / _partial.
 bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv,
                        uint32_t head_dim, bml_dtype dt, float scale, const float *q, float *out, float *pm,
@@ -397,9 +338,6 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
 
     const float sc = resolve_scale(scale, head_dim);
     const size_t es = bml::dtype_size(dt);
-    if (kUseTensorCoreDecode && bml::decode_tc_supported(dt, head_dim, n_heads / n_kv))
-        return decode_tc_impl(seqs, n_seqs, n_heads, n_kv, head_dim, dt, sc, q, out, pm, pl, po, ws, sms, stream,
-                              mode, fn);
     const uint32_t T = bml::decode_rows_per_tile(dt, head_dim, n_kv);
     static thread_local bml::DecodeParams p;  // ~8 KB, kept off the stack
     for (uint32_t base = 0; base < n_seqs; base += bml::kMaxSeqsPerLaunch) {
