@@ -61,14 +61,14 @@ def load_peaks():
 
 def decode_kernel_name(kv_dtype, head_dim: int, n_kv: int, group: int) -> str:
     """Kernel that bml_attn_decode_batched launches for a shape: the
-    warp-MMA kernel for 16-bit caches with 512..2048-byte position rows, the
-    CUDA-core kernel otherwise (mirrors decode_mma_supported in
-    bml_b200/csrc/decode_mma.cu)."""
+    warp-MMA kernel with TMA loads for 16-bit caches with 512..2048-byte
+    position rows, the CUDA-core kernel otherwise (mirrors
+    decode_mma_supported in bml_b200/csrc/decode_mma.cu)."""
     import torch
     row = n_kv * head_dim * 2
     mma = (kv_dtype in (torch.float16, torch.bfloat16) and head_dim in (64, 128) and group in (1, 2, 4, 8)
            and n_kv in (1, 2, 4, 8) and 512 <= row <= 2048)
-    return "decode_mma_kernel" if mma else "decode_kernel"
+    return "decode_tma_kernel" if mma else "decode_kernel"
 
 
 def profile_traffic(name: str):

@@ -340,8 +340,12 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
     const size_t es = bml::dtype_size(dt);
     const uint32_t T = bml::decode_rows_per_tile(dt, head_dim, n_kv);
     static thread_local bml::DecodeParams p;  // ~8 KB, kept off the stack
-    for (uint32_t base = 0; base < n_seqs; base += bml::kMaxSeqsPerLaunch) {
-        const uint32_t ns = std::min<uint32_t>(n_seqs - base, bml::kMaxSeqsPerLaunch);
+    // the TMA kernel carries two tensor maps per sequence in its parameters
+    const uint32_t chunk = bml::decode_tma_supported(dt, head_dim, n_kv, n_heads / n_kv)
+                               ? bml::decode_tma_max_seqs()
+                               : (uint32_t)bml::kMaxSeqsPerLaunch;
+    for (uint32_t base = 0; base < n_seqs; base += chunk) {
+        const uint32_t ns = std::min<uint32_t>(n_seqs - base, chunk);
         memset(&p, 0, offsetof(bml::DecodeParams, seqs));
         uint64_t total = 0;
         for (uint32_t s = 0; s < ns; ++s) total += (seqs[base + s].len + T - 1) / T;

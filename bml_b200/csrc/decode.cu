@@ -692,8 +692,13 @@ bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_
 
 cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                           int grid, cudaStream_t stream) {
-    // 16-bit caches of the common shapes take the tensor-core kernel
-    // (decode_mma.cu); everything else the CUDA-core kernel below.
+    // 16-bit caches of the common shapes take the tensor-core kernels (TMA
+    // loads in decode_tma.cu, else cp.async loads in decode_mma.cu);
+    // everything else the CUDA-core kernel below.
+    if (p.n_seqs <= decode_tma_max_seqs() && decode_tma_supported(dt, head_dim, p.n_kv, group)) {
+        const cudaError_t e = launch_decode_tma(p, dt, head_dim, group, grid, stream);
+        if (e != cudaErrorNotSupported) return e;
+    }
     if (decode_mma_supported(dt, head_dim, p.n_kv, group))
         return launch_decode_mma(p, dt, head_dim, group, grid, stream);
     switch (dt) {

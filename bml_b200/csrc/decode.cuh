@@ -74,6 +74,15 @@ bool decode_mma_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32
 cudaError_t launch_decode_mma(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                               int grid, cudaStream_t stream);
 
+// Same arithmetic with K/V brought in by TMA through per-sequence tensor
+// maps (decode_tma.cu); at most decode_tma_max_seqs() sequences a launch.
+// launch_decode prefers it where supported; cudaErrorNotSupported means the
+// caller should fall back.
+bool decode_tma_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
+uint32_t decode_tma_max_seqs();
+cudaError_t launch_decode_tma(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
+                              int grid, cudaStream_t stream);
+
 // Merge of split-K slots for sequences spread over more CTAs than the
 // in-kernel merge handles well; one CTA per (sequence, head) row.
 cudaError_t launch_slot_merge(const DecodeParams &p, uint32_t head_dim, cudaStream_t stream);
