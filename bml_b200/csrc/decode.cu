@@ -30,6 +30,8 @@
 //    last CTA to finish that sequence (atomic ticket, reset afterwards)
 //    merges them with the log-sum-exp rule in slot order.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "decode.cuh"
 
@@ -690,16 +692,27 @@ bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_
     return true;
 }
 
+DecodeFamily decode_family_override() {
+    static const DecodeFamily fam = [] {
+        const char *v = getenv("BML_DECODE_KERNEL");
+        if (v && strcmp(v, "mma") == 0) return kDecodeMma;
+        if (v && strcmp(v, "cuda") == 0) return kDecodeCuda;
+        return kDecodeTma;
+    }();
+    return fam;
+}
+
 cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                           int grid, cudaStream_t stream) {
     // 16-bit caches of the common shapes take the tensor-core kernels (TMA
     // loads in decode_tma.cu, else cp.async loads in decode_mma.cu);
     // everything else the CUDA-core kernel below.
-    if (p.n_seqs <= decode_tma_max_seqs() && decode_tma_supported(dt, head_dim, p.n_kv, group)) {
+    const DecodeFamily fam = decode_family_override();
+    if (fam == kDecodeTma && p.n_seqs <= decode_tma_max_seqs() && decode_tma_supported(dt, head_dim, p.n_kv, group)) {
         const cudaError_t e = launch_decode_tma(p, dt, head_dim, group, grid, stream);
         if (e != cudaErrorNotSupported) return e;
     }
-    if (decode_mma_supported(dt, head_dim, p.n_kv, group))
+    if (fam != kDecodeCuda && decode_mma_supported(dt, head_dim, p.n_kv, group))
         return launch_decode_mma(p, dt, head_dim, group, grid, stream);
     switch (dt) {
         case BML_F32: return launch_d<float>(p, head_dim, group, grid, stream);

@@ -80,6 +80,13 @@ cudaError_t launch_decode_mma(const DecodeParams &p, bml_dtype dt, uint32_t head
 // caller should fall back.
 bool decode_tma_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
 uint32_t decode_tma_max_seqs();
+
+// Kernel family the library uses for 16-bit caches; BML_DECODE_KERNEL=mma
+// or =cuda in the environment (read once) selects the cp.async warp-MMA
+// kernel or the CUDA-core kernel instead of the TMA one -- for tests and
+// comparisons.
+enum DecodeFamily : int { kDecodeTma = 0, kDecodeMma = 1, kDecodeCuda = 2 };
+DecodeFamily decode_family_override();
 cudaError_t launch_decode_tma(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                               int grid, cudaStream_t stream);
 
