@@ -42,6 +42,8 @@ sys.path.insert(0, ROOT)
 
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# nominal B200 figures, reported beside the measured-peak fractions
+SPEC_PEAKS = {"hbm_gbs": 8000.0, "bf16_tflops": 2250.0}
 
 DECODE_METRIC = "GQA decode-attn HBM GB/s (% peak) + prefill TFLOP/s"
 
@@ -291,14 +293,14 @@ def decode_step_bytes(batch, n_heads):
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle) on a bounded sample
 # ---------------------------------------------------------------------------
-def cpu_decode_sample(workload: str, budget_s: float):
-    """Times the oracle (all host threads) on a bounded sample of the
-    workload; returns (GB/s, threads, description)."""
+def cpu_decode_sample(workload: str, budget_s: float, threads: int = 0):
+    """Times the oracle (all host threads, or `threads`) on a bounded sample
+    of the workload; returns (GB/s, threads, description)."""
     import numpy as np
 
     import oracle
     from bml_b200 import workloads as W
-    threads = host_threads()
+    threads = threads or host_threads()
     if workload == "batched_tinyllama":
         q, ks, vs = W.batched_tinyllama(n_seqs=8)
         code, nkv, d, es = None, 4, 64, 2
@@ -380,7 +382,7 @@ def run_prefill(dev, steps, warmup, dist, peaks, n=4, S=8192):
             "config": {"workload": "llama3_prefill", "n_seqs": n, "seq_len": S, "n_heads": H,
                        "n_kv_heads": Hkv, "head_dim": d, "causal": True, "dtype": "bf16"},
             "roofline": {"bound": "tensor", "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(ach / peak, 4),
+                         "frac": round(ach / peak, 4), "frac_spec": round(ach / SPEC_PEAKS["bf16_tflops"], 4),
                          "traffic": profile_traffic("prefill_tcgen05_llama3.txt")},
             "clocks": clocks}
 
@@ -443,7 +445,8 @@ def run_b200(args):
         "metric": DECODE_METRIC, "value": round(gbs, 1), "unit": "GB/s",
         "ms_per_step": round(ms / args.steps, 5), "scaling": scaling, "dtype": dtype, "config": cfg,
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(ach / hbm, 4), "traffic": profile_traffic(f"decode_{wl}.txt"),
+                     "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
+                     "traffic": profile_traffic(f"decode_{wl}.txt"),
                      "kernel": decode_kernel_name(batch.dtype, batch.head_dim, batch.n_kv, H // batch.n_kv),
                      "kernel_ms": round(kms, 5),
                      "algorithmic_bytes_per_launch": step_bytes},
@@ -454,9 +457,10 @@ def run_b200(args):
         res["prefill"] = pre
         res["gpu_launches"] += pre.get("steps", 0)
     if dist.world == 1 and not args.no_cpu:
-        v, thr, desc = cpu_decode_sample(wl, args.cpu_budget)
+        v, thr, desc = cpu_decode_sample(wl, args.cpu_budget * 0.7)
+        v1, _, desc1 = cpu_decode_sample(wl, args.cpu_budget * 0.3, threads=1)
         res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
-                               "sample": desc}
+                               "sample": desc, "value_1core": round(v1, 4), "sample_1core": desc1}
         if "prefill" in res and "value" in res["prefill"]:
             pv, pthr, pdesc = cpu_prefill_sample(args.cpu_budget / 2)
             res["prefill"]["cpu_baseline"] = {"value": round(pv, 5), "unit": "TFLOP/s", "cores": pthr,
@@ -536,7 +540,8 @@ def run_longctx(args, dist, peaks, res):
                                                    "(m, l, o) + LSE merge",
                            "l2": "256 MiB of KV per step on 1 GPU"},
                 "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                             "frac": round(ach / hbm, 4), "traffic": profile_traffic("decode_longctx.txt"),
+                             "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
+                             "traffic": profile_traffic("decode_longctx.txt"),
                              "kernel": decode_kernel_name(torch.bfloat16, d, Hkv, H // Hkv),
                              "kernel_ms": round(kms, 5)},
                 "clocks": clocks, "gpu_launches": args.steps * (1 if dist.world == 1 else 2)})
