@@ -291,6 +291,27 @@ BML_API bml_status bml_kv_append(bml_kv *kv, uint32_t layer, uint32_t pos, const
     return ok();
 }
 
+BML_API bml_status bml_kv_append_rope(bml_kv *kv, uint32_t layer, uint32_t pos, float *q_dev, uint32_t n_heads,
+                                      const float *k_dev, const float *v_dev, void *stream) {
+    size_t off = 0;
+    bml_status st = check_slot(kv, BML_WHICH_K, layer, pos, 0, "bml_kv_append_rope", &off);
+    if (st != BML_OK) return st;
+    if (!q_dev || !k_dev || !v_dev) return fail(BML_E_INVALID, "bml_kv_append_rope: null argument");
+    const uint32_t n_kv = kv->desc.n_kv_heads, d = kv->desc.head_dim;
+    if (n_heads == 0 || n_heads % n_kv != 0)
+        return fail(BML_E_INVALID, "bml_kv_append_rope: n_heads %u not a multiple of n_kv_heads %u", n_heads, n_kv);
+    if (d % 2 != 0) return fail(BML_E_INVALID, "bml_kv_append_rope: head_dim %u is odd", d);
+    DeviceGuard g(kv->desc.device);
+    char *kd = static_cast<char *>(kv->k[layer]) + off * kv->esize();
+    char *vd = static_cast<char *>(kv->v[layer]) + off * kv->esize();
+    CUDA_TRY(bml::kv_rope_append(q_dev, n_heads, k_dev, v_dev, kd, vd, kv->desc.dtype, n_kv, d, pos,
+                                 static_cast<cudaStream_t>(stream)),
+             "bml_kv_append_rope");
+    kv->n_total_k += n_kv;
+    kv->n_total_v += n_kv;
+    return ok();
+}
+
 // ---------------------------------------------------------------------------
 // Decode
 // ---------------------------------------------------------------------------

@@ -118,7 +118,64 @@ __global__ void diag_exp2_kernel(const float2 *__restrict__ x, uint32_t n2, int 
     out[i] = method == 1 ? exp2_poly2(v) : make_float2(fast_exp2(v.x), fast_exp2(v.y));
 }
 
+// RoPE of gguf_compiler.rs:1290-1317 (interleaved pairs (2i, 2i+1) of each
+// head, angle = pos * 10000^(-2i/d), rotation in f64) on q (in place) and k,
+// then k and v stored into a cache slot -- the projection tail of
+// gguf_compiler.rs:984-1006 for one token.  One thread per q pair, k pair
+// and v element.  f32 -> f64 -> rotate -> f32 (as the reference's f64
+// vectors land in its f32 cache) -> cache dtype.
+template <typename Dt>
+__global__ void rope_append_kernel(float *__restrict__ q, uint32_t nq2, const float *__restrict__ k,
+                                   const float *__restrict__ v, Dt *__restrict__ kd, Dt *__restrict__ vd,
+                                   uint32_t nk2, uint32_t nv, uint32_t d, uint32_t pos) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t half = d / 2;
+    if (i < nq2 + nk2) {
+        const bool is_q = i < nq2;
+        const uint32_t pi = is_q ? i : i - nq2;  // pair index
+        const uint32_t j = pi % half;            // pair within the head
+        const uint32_t e = (pi / half) * d + 2 * j;
+        const float *src = is_q ? q : k;
+        const double xe = (double)src[e], xo = (double)src[e + 1];
+        const double freq = 1.0 / pow(10000.0, 2.0 * (double)j / (double)d);
+        double sn, cs;
+        sincos((double)pos * freq, &sn, &cs);
+        const float re = (float)(xe * cs - xo * sn);
+        const float ro = (float)(xe * sn + xo * cs);
+        if (is_q) {
+            q[e] = re;
+            q[e + 1] = ro;
+        } else {
+            kd[e] = from_f32<Dt>(re);
+            kd[e + 1] = from_f32<Dt>(ro);
+        }
+    } else if (i < nq2 + nk2 + nv) {
+        const uint32_t e = i - nq2 - nk2;
+        vd[e] = from_f32<Dt>(v[e]);
+    }
+}
+
 }  // namespace
+
+cudaError_t kv_rope_append(float *q, uint32_t n_heads, const float *k, const float *v, void *kd, void *vd,
+                           bml_dtype dst_t, uint32_t n_kv, uint32_t d, uint32_t pos, cudaStream_t st) {
+    const uint32_t nq2 = n_heads * d / 2, nk2 = n_kv * d / 2, nv = n_kv * d;
+    const uint32_t total = nq2 + nk2 + nv;
+    const unsigned blocks = (total + 255) / 256;
+    switch (dst_t) {
+        case BML_F32:
+            rope_append_kernel<float><<<blocks, 256, 0, st>>>(q, nq2, k, v, (float *)kd, (float *)vd, nk2, nv, d, pos);
+            break;
+        case BML_F16:
+            rope_append_kernel<__half><<<blocks, 256, 0, st>>>(q, nq2, k, v, (__half *)kd, (__half *)vd, nk2, nv, d, pos);
+            break;
+        case BML_BF16:
+            rope_append_kernel<__nv_bfloat16>
+                <<<blocks, 256, 0, st>>>(q, nq2, k, v, (__nv_bfloat16 *)kd, (__nv_bfloat16 *)vd, nk2, nv, d, pos);
+            break;
+    }
+    return cudaGetLastError();
+}
 
 cudaError_t diag_exp2(const float *x, uint32_t n, int method, float *out, cudaStream_t st) {
     if (n == 0) return cudaSuccess;

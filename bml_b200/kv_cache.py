@@ -137,6 +137,23 @@ class HashConsedKV:
         L.call("bml_kv_append", self._h, layer, pos, _ptr(k), _ptr(v), dtype_code(k.dtype),
                _stream(stream))
 
+    def append_rope(self, layer: int, pos: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                    stream=None) -> torch.Tensor:
+        """RoPE on q (in place) and k, then k and v stored at pos: the
+        projection tail of gguf_compiler.rs:984-1006 with apply_rope_inplace
+        (:1290-1317) in one launch.  q [n_heads, head_dim], k/v [n_kv_heads,
+        head_dim], all f32 CUDA tensors; returns q."""
+        _need(q, "q", torch.float32)
+        _need(k, "k", torch.float32)
+        _need(v, "v", torch.float32)
+        if k.numel() != self.n_kv_heads * self.head_dim or v.numel() != k.numel():
+            raise ValueError("k/v must hold n_kv_heads * head_dim values")
+        if q.numel() % self.head_dim != 0:
+            raise ValueError("q must hold n_heads * head_dim values")
+        L.call("bml_kv_append_rope", self._h, layer, pos, _ptr(q), q.numel() // self.head_dim, _ptr(k), _ptr(v),
+               _stream(stream))
+        return q
+
     def attention(self, q: torch.Tensor, layer: int, pos: int, scale: float = -1.0,
                   out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         """The attention block of forward_layer_cached (gguf_compiler.rs:

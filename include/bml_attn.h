@@ -133,6 +133,18 @@ bml_status bml_kv_append(bml_kv *kv, uint32_t layer, uint32_t pos,
                          const void *k_dev, const void *v_dev,
                          bml_dtype src_dtype, void *stream);
 
+/* The projection tail of one token in one launch (gguf_compiler.rs:984-1006
+ * with apply_rope_inplace, :1290-1317): RoPE -- interleaved pairs
+ * (2i, 2i+1) of each head, angle = pos * 10000^(-2i/head_dim), rotated in
+ * f64 -- applied to q in place and to k, then k and v stored into the slot
+ * of `pos` like bml_kv_append.  q_dev: [n_heads][head_dim] f32 (n_heads a
+ * multiple of n_kv_heads); k_dev (before RoPE), v_dev:
+ * [n_kv_heads][head_dim] f32.  Asynchronous on stream. */
+bml_status bml_kv_append_rope(bml_kv *kv, uint32_t layer, uint32_t pos,
+                              float *q_dev, uint32_t n_heads,
+                              const float *k_dev, const float *v_dev,
+                              void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Decode attention  (gguf_compiler.rs:1008-1050)                           */
 /* ------------------------------------------------------------------------ */
