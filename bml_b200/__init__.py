@@ -11,8 +11,11 @@ package is its host-side mirror of the reference interface:
   prefill            the forward_cached token loop, gguf_compiler.rs:946-958
   decode_partial / merge_lse
                      KV-split flash decoding (no reference counterpart)
+  DecodeBatcher      continuous batching of decode steps, the batched form
+                     of crates/api/src/main.rs:266-354's one-request loop
 """
 from ._lib import BmlError, BmlInvalid, BmlUnsupported, last_error  # noqa: F401
 from .attention import (SeqBatch, Workspace, decode_batched, decode_partial,  # noqa: F401
                         merge_lse, merge_lse_packed, prefill, softmax_f32)
 from .kv_cache import HashConsedKV  # noqa: F401
+from .batching import AtCapacity, DecodeBatcher, MAX_PENDING_REQUESTS  # noqa: F401

@@ -312,6 +312,72 @@ BML_API bml_status bml_kv_append_rope(bml_kv *kv, uint32_t layer, uint32_t pos, 
     return ok();
 }
 
+namespace {
+
+// Fills p with the destinations of seqs_host[base, base + ns) of a batched
+// append; a null buffer is an error.
+bml_status fill_append_rows(bml::AppendRows &p, const bml_seq_desc *seqs_host, uint32_t base, uint32_t ns,
+                            const char *fn) {
+    for (uint32_t i = 0; i < ns; ++i) {
+        const bml_seq_desc &d = seqs_host[base + i];
+        if (!d.k_dev || !d.v_dev) return fail(BML_E_INVALID, "%s: sequence %u has a null buffer", fn, base + i);
+        p.k[i] = const_cast<void *>(d.k_dev);
+        p.v[i] = const_cast<void *>(d.v_dev);
+        p.len[i] = d.len;
+    }
+    return BML_OK;
+}
+
+}  // namespace
+
+BML_API bml_status bml_kv_append_batched(const bml_seq_desc *seqs_host, uint32_t n_seqs, uint32_t n_kv_heads,
+                                         uint32_t head_dim, bml_dtype kv_dtype, const void *k_new_dev,
+                                         const void *v_new_dev, bml_dtype src_dtype, void *stream) {
+    const char *fn = "bml_kv_append_batched";
+    if (!seqs_host || !k_new_dev || !v_new_dev) return fail(BML_E_INVALID, "%s: null argument", fn);
+    if (!valid_dtype(kv_dtype) || !valid_dtype(src_dtype)) return fail(BML_E_INVALID, "%s: bad dtype", fn);
+    if (n_kv_heads == 0 || head_dim == 0) return fail(BML_E_INVALID, "%s: zero dimension", fn);
+    static thread_local bml::AppendRows p;  // ~5 KB, kept off the stack
+    p.row = n_kv_heads * head_dim;
+    p.n_heads = 0;
+    p.head_dim = head_dim;
+    const size_t src_row = (size_t)p.row * bml::dtype_size(src_dtype);
+    for (uint32_t base = 0; base < n_seqs; base += bml::kMaxAppendSeqs) {
+        const uint32_t ns = std::min<uint32_t>(n_seqs - base, bml::kMaxAppendSeqs);
+        if (bml_status st = fill_append_rows(p, seqs_host, base, ns, fn)) return st;
+        CUDA_TRY(bml::kv_append_rows(p, ns, static_cast<const char *>(k_new_dev) + base * src_row,
+                                     static_cast<const char *>(v_new_dev) + base * src_row, src_dtype, kv_dtype,
+                                     static_cast<cudaStream_t>(stream)),
+                 fn);
+    }
+    return ok();
+}
+
+BML_API bml_status bml_kv_append_rope_batched(const bml_seq_desc *seqs_host, uint32_t n_seqs, uint32_t n_heads,
+                                              uint32_t n_kv_heads, uint32_t head_dim, bml_dtype kv_dtype,
+                                              float *q_dev, const float *k_new_dev, const float *v_new_dev,
+                                              void *stream) {
+    const char *fn = "bml_kv_append_rope_batched";
+    if (!seqs_host || !q_dev || !k_new_dev || !v_new_dev) return fail(BML_E_INVALID, "%s: null argument", fn);
+    if (!valid_dtype(kv_dtype)) return fail(BML_E_INVALID, "%s: bad dtype", fn);
+    if (n_kv_heads == 0 || head_dim == 0 || n_heads == 0) return fail(BML_E_INVALID, "%s: zero dimension", fn);
+    if (n_heads % n_kv_heads) return fail(BML_E_INVALID, "%s: n_heads %% n_kv_heads != 0", fn);
+    if (head_dim % 2) return fail(BML_E_INVALID, "%s: RoPE needs an even head_dim", fn);
+    static thread_local bml::AppendRows p;
+    p.row = n_kv_heads * head_dim;
+    p.n_heads = n_heads;
+    p.head_dim = head_dim;
+    for (uint32_t base = 0; base < n_seqs; base += bml::kMaxAppendSeqs) {
+        const uint32_t ns = std::min<uint32_t>(n_seqs - base, bml::kMaxAppendSeqs);
+        if (bml_status st = fill_append_rows(p, seqs_host, base, ns, fn)) return st;
+        CUDA_TRY(bml::kv_rope_append_rows(p, ns, q_dev + (size_t)base * n_heads * head_dim,
+                                          k_new_dev + (size_t)base * p.row, v_new_dev + (size_t)base * p.row,
+                                          kv_dtype, static_cast<cudaStream_t>(stream)),
+                 fn);
+    }
+    return ok();
+}
+
 // ---------------------------------------------------------------------------
 // Decode
 // ---------------------------------------------------------------------------

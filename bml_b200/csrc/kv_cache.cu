@@ -124,6 +124,19 @@ __global__ void diag_exp2_kernel(const float2 *__restrict__ x, uint32_t n2, int 
 // gguf_compiler.rs:984-1006 for one token.  One thread per q pair, k pair
 // and v element.  f32 -> f64 -> rotate -> f32 (as the reference's f64
 // vectors land in its f32 cache) -> cache dtype.
+// RoPE of one interleaved pair (x[2j], x[2j+1]) of a head at position pos:
+// angle pos * 10000^(-2j/d), rotated in f64 and rounded to f32 once
+// (gguf_compiler.rs:1290-1317 computes in f64 and stores f32).
+__device__ __forceinline__ void rope_pair(float xe_f, float xo_f, uint32_t j, uint32_t d, uint32_t pos,
+                                          float &re, float &ro) {
+    const double xe = (double)xe_f, xo = (double)xo_f;
+    const double freq = 1.0 / pow(10000.0, 2.0 * (double)j / (double)d);
+    double sn, cs;
+    sincos((double)pos * freq, &sn, &cs);
+    re = (float)(xe * cs - xo * sn);
+    ro = (float)(xe * sn + xo * cs);
+}
+
 template <typename Dt>
 __global__ void rope_append_kernel(float *__restrict__ q, uint32_t nq2, const float *__restrict__ k,
                                    const float *__restrict__ v, Dt *__restrict__ kd, Dt *__restrict__ vd,
@@ -136,12 +149,8 @@ __global__ void rope_append_kernel(float *__restrict__ q, uint32_t nq2, const fl
         const uint32_t j = pi % half;            // pair within the head
         const uint32_t e = (pi / half) * d + 2 * j;
         const float *src = is_q ? q : k;
-        const double xe = (double)src[e], xo = (double)src[e + 1];
-        const double freq = 1.0 / pow(10000.0, 2.0 * (double)j / (double)d);
-        double sn, cs;
-        sincos((double)pos * freq, &sn, &cs);
-        const float re = (float)(xe * cs - xo * sn);
-        const float ro = (float)(xe * sn + xo * cs);
+        float re, ro;
+        rope_pair(src[e], src[e + 1], j, d, pos, re, ro);
         if (is_q) {
             q[e] = re;
             q[e + 1] = ro;
@@ -155,7 +164,94 @@ __global__ void rope_append_kernel(float *__restrict__ q, uint32_t nq2, const fl
     }
 }
 
+// Row `len_i` of each sequence i of a batch gets that sequence's new K and V
+// (one decode step's appends for a whole batch in one launch).
+template <typename S, typename Dt>
+__global__ void append_rows_kernel(const __grid_constant__ AppendRows p, const S *__restrict__ k_src,
+                                   const S *__restrict__ v_src) {
+    const uint32_t s = blockIdx.y;
+    const size_t n = p.row;
+    Dt *kd = static_cast<Dt *>(p.k[s]) + (size_t)p.len[s] * n;
+    Dt *vd = static_cast<Dt *>(p.v[s]) + (size_t)p.len[s] * n;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        kd[i] = from_f32<Dt>(to_f32<S>(k_src[(size_t)s * n + i]));
+        vd[i] = from_f32<Dt>(to_f32<S>(v_src[(size_t)s * n + i]));
+    }
+}
+
+// The batched form of rope_append_kernel: sequence blockIdx.y rotates its q
+// rows in place and its k row at position len[s], then stores k and v into
+// row len[s] of its cache.
+template <typename Dt>
+__global__ void rope_append_rows_kernel(const __grid_constant__ AppendRows p, float *__restrict__ q,
+                                        const float *__restrict__ k_src, const float *__restrict__ v_src) {
+    const uint32_t s = blockIdx.y;
+    const uint32_t d = p.head_dim, half = d / 2, pos = p.len[s];
+    const uint32_t nq2 = p.n_heads * half, nk2 = p.row / 2, nv = p.row;
+    float *qs = q + (size_t)s * p.n_heads * d;
+    const float *ks = k_src + (size_t)s * p.row, *vs = v_src + (size_t)s * p.row;
+    Dt *kd = static_cast<Dt *>(p.k[s]) + (size_t)pos * p.row;
+    Dt *vd = static_cast<Dt *>(p.v[s]) + (size_t)pos * p.row;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nq2 + nk2 + nv; i += gridDim.x * blockDim.x) {
+        if (i < nq2 + nk2) {
+            const bool is_q = i < nq2;
+            const uint32_t pi = is_q ? i : i - nq2;
+            const uint32_t j = pi % half, e = (pi / half) * d + 2 * j;
+            float re, ro;
+            rope_pair(is_q ? qs[e] : ks[e], is_q ? qs[e + 1] : ks[e + 1], j, d, pos, re, ro);
+            if (is_q) {
+                qs[e] = re;
+                qs[e + 1] = ro;
+            } else {
+                kd[e] = from_f32<Dt>(re);
+                kd[e + 1] = from_f32<Dt>(ro);
+            }
+        } else {
+            const uint32_t e = i - nq2 - nk2;
+            vd[e] = from_f32<Dt>(vs[e]);
+        }
+    }
+}
+
+template <typename S>
+cudaError_t append_rows_to(const AppendRows &p, const void *k, const void *v, bml_dtype dst_t, dim3 grid,
+                           cudaStream_t st) {
+    switch (dst_t) {
+        case BML_F32: append_rows_kernel<S, float><<<grid, 256, 0, st>>>(p, (const S *)k, (const S *)v); break;
+        case BML_F16: append_rows_kernel<S, __half><<<grid, 256, 0, st>>>(p, (const S *)k, (const S *)v); break;
+        case BML_BF16:
+            append_rows_kernel<S, __nv_bfloat16><<<grid, 256, 0, st>>>(p, (const S *)k, (const S *)v);
+            break;
+    }
+    return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t kv_append_rows(const AppendRows &p, uint32_t n_seqs, const void *k, const void *v, bml_dtype src_t,
+                           bml_dtype dst_t, cudaStream_t st) {
+    if (n_seqs == 0) return cudaSuccess;
+    const dim3 grid((unsigned)((p.row + 255) / 256 < 64 ? (p.row + 255) / 256 : 64), n_seqs);
+    switch (src_t) {
+        case BML_F32: return append_rows_to<float>(p, k, v, dst_t, grid, st);
+        case BML_F16: return append_rows_to<__half>(p, k, v, dst_t, grid, st);
+        case BML_BF16: return append_rows_to<__nv_bfloat16>(p, k, v, dst_t, grid, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t kv_rope_append_rows(const AppendRows &p, uint32_t n_seqs, float *q, const float *k, const float *v,
+                                bml_dtype dst_t, cudaStream_t st) {
+    if (n_seqs == 0) return cudaSuccess;
+    const uint32_t total = p.n_heads * p.head_dim / 2 + p.row / 2 + p.row;
+    const dim3 grid((total + 255) / 256 < 32 ? (total + 255) / 256 : 32, n_seqs);
+    switch (dst_t) {
+        case BML_F32: rope_append_rows_kernel<float><<<grid, 256, 0, st>>>(p, q, k, v); break;
+        case BML_F16: rope_append_rows_kernel<__half><<<grid, 256, 0, st>>>(p, q, k, v); break;
+        case BML_BF16: rope_append_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(p, q, k, v); break;
+    }
+    return cudaGetLastError();
+}
 
 cudaError_t kv_rope_append(float *q, uint32_t n_heads, const float *k, const float *v, void *kd, void *vd,
                            bml_dtype dst_t, uint32_t n_kv, uint32_t d, uint32_t pos, cudaStream_t st) {

@@ -169,6 +169,32 @@ typedef struct bml_seq_desc {
     uint32_t reserved;
 } bml_seq_desc;
 
+/* One decode step's appends for a batch of caller-owned caches (the
+ * per-request store_k/store_v of gguf_compiler.rs:994-1006, batched; no
+ * reference counterpart -- the reference serves one request at a time):
+ * writes row seqs[i].len of sequence i ([capacity][n_kv_heads][head_dim]
+ * buffers in kv_dtype, writable, room for that row is the caller's) from
+ * k_new_dev / v_new_dev [n_seqs][n_kv_heads][head_dim] in src_dtype.  The
+ * caller then advances each len.  Asynchronous on stream. */
+bml_status bml_kv_append_batched(const bml_seq_desc *seqs_host, uint32_t n_seqs,
+                                 uint32_t n_kv_heads, uint32_t head_dim,
+                                 bml_dtype kv_dtype, const void *k_new_dev,
+                                 const void *v_new_dev, bml_dtype src_dtype,
+                                 void *stream);
+
+/* bml_kv_append_batched with the RoPE of bml_kv_append_rope: sequence i's q
+ * rows ([n_seqs][n_heads][head_dim] f32, rotated in place) and its new k row
+ * are rotated for position seqs[i].len, then k and v ([n_seqs][n_kv_heads]
+ * [head_dim] f32) are stored into row seqs[i].len of its caches.  The
+ * per-request RoPE + store of gguf_compiler.rs:984-1006 and :1290-1317 for
+ * a whole batch in one launch.  Asynchronous on stream. */
+bml_status bml_kv_append_rope_batched(const bml_seq_desc *seqs_host,
+                                      uint32_t n_seqs, uint32_t n_heads,
+                                      uint32_t n_kv_heads, uint32_t head_dim,
+                                      bml_dtype kv_dtype, float *q_dev,
+                                      const float *k_new_dev,
+                                      const float *v_new_dev, void *stream);
+
 /* Scratch bytes bml_attn_decode_batched / _partial need for n_seqs
  * sequences on `device`. */
 bml_status bml_attn_decode_workspace_size(uint32_t n_seqs, uint32_t n_heads,
