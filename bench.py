@@ -61,16 +61,19 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
-def decode_kernel_name(kv_dtype, head_dim: int, n_kv: int, group: int) -> str:
+def decode_kernel_name(kv_dtype, head_dim: int, n_kv: int, group: int, n_seqs: int) -> str:
     """Kernel that bml_attn_decode_batched launches for a shape: the
-    warp-MMA kernel with TMA loads for 16-bit caches with 512..2048-byte
-    position rows, the CUDA-core kernel otherwise (mirrors
-    decode_mma_supported in bml_b200/csrc/decode_mma.cu)."""
+    warp-MMA kernels for 16-bit caches with 512..2048-byte position rows --
+    TMA loads for up to 64 sequences, bulk copies for more -- and the
+    CUDA-core kernel otherwise (mirrors launch_decode in
+    bml_b200/csrc/decode.cu)."""
     import torch
     row = n_kv * head_dim * 2
     mma = (kv_dtype in (torch.float16, torch.bfloat16) and head_dim in (64, 128) and group in (1, 2, 4, 8)
            and n_kv in (1, 2, 4, 8) and 512 <= row <= 2048)
-    return "decode_tma_kernel" if mma else "decode_kernel"
+    if not mma:
+        return "decode_kernel"
+    return "decode_tma_kernel" if n_seqs <= 64 else "decode_bulk_kernel"
 
 
 def profile_traffic(name: str):
@@ -447,7 +450,7 @@ def run_b200(args):
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
                      "traffic": profile_traffic(f"decode_{wl}.txt"),
-                     "kernel": decode_kernel_name(batch.dtype, batch.head_dim, batch.n_kv, H // batch.n_kv),
+                     "kernel": decode_kernel_name(batch.dtype, batch.head_dim, batch.n_kv, H // batch.n_kv, len(batch)),
                      "kernel_ms": round(kms, 5),
                      "algorithmic_bytes_per_launch": step_bytes},
         "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps,
@@ -542,7 +545,7 @@ def run_longctx(args, dist, peaks, res):
                 "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                              "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
                              "traffic": profile_traffic("decode_longctx.txt"),
-                             "kernel": decode_kernel_name(torch.bfloat16, d, Hkv, H // Hkv),
+                             "kernel": decode_kernel_name(torch.bfloat16, d, Hkv, H // Hkv, 1),
                              "kernel_ms": round(kms, 5)},
                 "clocks": clocks, "gpu_launches": args.steps * (1 if dist.world == 1 else 2)})
     if dist.world == 1 and not args.no_cpu:

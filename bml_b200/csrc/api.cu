@@ -427,7 +427,9 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
     const size_t es = bml::dtype_size(dt);
     const uint32_t T = bml::decode_rows_per_tile(dt, head_dim, n_kv);
     static thread_local bml::DecodeParams p;  // ~8 KB, kept off the stack
-    // the TMA kernel carries two tensor maps per sequence in its parameters
+    // the TMA kernel carries two tensor maps per sequence in its parameters:
+    // when it is forced, launches take at most its 64 sequences (by default
+    // larger launches go to the bulk-copy kernel)
     const uint32_t chunk = bml::decode_family_override() == bml::kDecodeTma &&
                                    bml::decode_tma_supported(dt, head_dim, n_kv, n_heads / n_kv)
                                ? bml::decode_tma_max_seqs()

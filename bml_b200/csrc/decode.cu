@@ -697,19 +697,29 @@ DecodeFamily decode_family_override() {
         const char *v = getenv("BML_DECODE_KERNEL");
         if (v && strcmp(v, "mma") == 0) return kDecodeMma;
         if (v && strcmp(v, "cuda") == 0) return kDecodeCuda;
-        return kDecodeTma;
+        if (v && strcmp(v, "bulk") == 0) return kDecodeBulk;
+        if (v && strcmp(v, "tma") == 0) return kDecodeTma;
+        return kDecodeAuto;
     }();
     return fam;
 }
 
 cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                           int grid, cudaStream_t stream) {
-    // 16-bit caches of the common shapes take the tensor-core kernels (TMA
-    // loads in decode_tma.cu, else cp.async loads in decode_mma.cu);
-    // everything else the CUDA-core kernel below.
+    // 16-bit caches of the common shapes take the tensor-core kernels: TMA
+    // tile loads (decode_tma.cu) for launches of up to 64 sequences, whole-
+    // group bulk copies (decode_bulk.cu) for larger ones, cp.async loads
+    // (decode_mma.cu) where neither applies; everything else the CUDA-core
+    // kernel below.
     const DecodeFamily fam = decode_family_override();
-    if (fam == kDecodeTma && p.n_seqs <= decode_tma_max_seqs() && decode_tma_supported(dt, head_dim, p.n_kv, group)) {
+    const bool tma_fits = p.n_seqs <= decode_tma_max_seqs();
+    if ((fam == kDecodeTma || (fam == kDecodeAuto && tma_fits)) && tma_fits &&
+        decode_tma_supported(dt, head_dim, p.n_kv, group)) {
         const cudaError_t e = launch_decode_tma(p, dt, head_dim, group, grid, stream);
+        if (e != cudaErrorNotSupported) return e;
+    }
+    if ((fam == kDecodeAuto || fam == kDecodeBulk) && decode_bulk_supported(dt, head_dim, p.n_kv, group)) {
+        const cudaError_t e = launch_decode_bulk(p, dt, head_dim, group, grid, stream);
         if (e != cudaErrorNotSupported) return e;
     }
     if (fam != kDecodeCuda && decode_mma_supported(dt, head_dim, p.n_kv, group))

@@ -81,11 +81,18 @@ cudaError_t launch_decode_mma(const DecodeParams &p, bml_dtype dt, uint32_t head
 bool decode_tma_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
 uint32_t decode_tma_max_seqs();
 
-// Kernel family the library uses for 16-bit caches; BML_DECODE_KERNEL=mma
-// or =cuda in the environment (read once) selects the cp.async warp-MMA
-// kernel or the CUDA-core kernel instead of the TMA one -- for tests and
-// comparisons.
-enum DecodeFamily : int { kDecodeTma = 0, kDecodeMma = 1, kDecodeCuda = 2 };
+// Same arithmetic with each cache row brought in by one 1-D bulk copy into
+// padded shared-memory rows (decode_bulk.cu); 256 sequences a launch.
+bool decode_bulk_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
+cudaError_t launch_decode_bulk(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
+                               int grid, cudaStream_t stream);
+
+// Kernel family for 16-bit caches.  By default (kDecodeAuto) a launch of at
+// most decode_tma_max_seqs() sequences takes the TMA kernel and a larger one
+// the bulk-copy kernel (one launch instead of several); BML_DECODE_KERNEL=tma,
+// =bulk, =mma or =cuda in the environment (read once) forces the TMA, bulk-
+// copy, cp.async warp-MMA or CUDA-core kernel -- for tests and comparisons.
+enum DecodeFamily : int { kDecodeAuto = 0, kDecodeMma = 1, kDecodeCuda = 2, kDecodeBulk = 3, kDecodeTma = 4 };
 DecodeFamily decode_family_override();
 cudaError_t launch_decode_tma(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                               int grid, cudaStream_t stream);

@@ -1,9 +1,10 @@
 """GPU parity of each decode kernel family for 16-bit caches.
 
-The library picks the TMA warp-MMA kernel for 16-bit caches; the cp.async
-warp-MMA kernel (its fallback) and the CUDA-core kernel are selected with
-BML_DECODE_KERNEL=mma / =cuda, which the library reads once per process, so
-each family runs in a child process.  Same oracle and 1e-4 tolerance as
+By default the library picks the TMA warp-MMA kernel for launches of up to
+64 sequences and the bulk-copy warp-MMA kernel for larger ones;
+BML_DECODE_KERNEL=tma / =bulk / =mma / =cuda forces one family (the
+cp.async warp-MMA kernel is the fallback of both), and the library reads it
+once per process, so each family runs in a child process.  Same oracle and 1e-4 tolerance as
 test_decode_gpu.py, on ragged lengths around every tile edge, more than 64
 sequences (the TMA kernel's per-launch limit) and a 2-slot split-K merge."""
 import os
@@ -53,7 +54,7 @@ print("WORST", worst)
 """
 
 
-@pytest.mark.parametrize("family", ["tma", "mma", "cuda"])
+@pytest.mark.parametrize("family", ["auto", "bulk", "tma", "mma", "cuda"])
 def test_decode_family_parity(cuda, family):
     env = dict(os.environ, BML_DECODE_KERNEL=family)
     res = subprocess.run([sys.executable, "-c", "ROOT = %r\n" % ROOT + CHILD], env=env, capture_output=True,
