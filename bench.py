@@ -19,6 +19,13 @@ is already resident in HBM.  Workloads (--workload):
                            NCCL and merged ("strong").
   llama3_prefill           causal prefill 4 x 8192, 32/8 heads, d=128,
                            bf16 operands (TFLOP/s of 4*d*H*causal pairs).
+  serving                  continuous batching (DecodeBatcher): 32 requests
+                           of Llama-3-8B shape (32 layers, 32/8 heads,
+                           d=128, bf16 KV), prompts U[1024,4096]; a step is
+                           one token of every request through all 32 layers
+                           (RoPE append + decode per layer); every 8 steps
+                           the longest request leaves and a new one joins.
+                           Metric: HBM GB/s of algorithmic bytes ("weak").
 
 The default decode line also carries a "prefill" object measured in the
 same run on the llama3_prefill workload.
@@ -61,19 +68,16 @@ def load_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
-def decode_kernel_name(kv_dtype, head_dim: int, n_kv: int, group: int, n_seqs: int) -> str:
+def decode_kernel_name(kv_dtype, head_dim: int, n_kv: int, group: int) -> str:
     """Kernel that bml_attn_decode_batched launches for a shape: the
-    warp-MMA kernels for 16-bit caches with 512..2048-byte position rows --
-    TMA loads for up to 64 sequences, bulk copies for more -- and the
-    CUDA-core kernel otherwise (mirrors launch_decode in
-    bml_b200/csrc/decode.cu)."""
+    bulk-copy warp-MMA kernel (dynamic schedule) for 16-bit caches with
+    512..2048-byte position rows, the CUDA-core kernel otherwise (mirrors
+    decode_select in bml_b200/csrc/decode.cu)."""
     import torch
     row = n_kv * head_dim * 2
     mma = (kv_dtype in (torch.float16, torch.bfloat16) and head_dim in (64, 128) and group in (1, 2, 4, 8)
            and n_kv in (1, 2, 4, 8) and 512 <= row <= 2048)
-    if not mma:
-        return "decode_kernel"
-    return "decode_tma_kernel" if n_seqs <= 64 else "decode_bulk_kernel"
+    return "decode_bulk_kernel" if mma else "decode_kernel"
 
 
 def profile_traffic(name: str):
@@ -425,6 +429,8 @@ def run_b200(args):
         dtype = "f32 (f16 KV)"
     elif wl == "longctx":
         return run_longctx(args, dist, peaks, res)
+    elif wl == "serving":
+        return run_serving(args, dist, peaks, res)
     else:
         raise SystemExit(f"unknown workload {wl}")
 
@@ -450,10 +456,13 @@ def run_b200(args):
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
                      "traffic": profile_traffic(f"decode_{wl}.txt"),
-                     "kernel": decode_kernel_name(batch.dtype, batch.head_dim, batch.n_kv, H // batch.n_kv, len(batch)),
+                     "kernel": decode_kernel_name(batch.dtype, batch.head_dim, batch.n_kv, H // batch.n_kv)
+                     + " + slot_merge_kernel",
                      "kernel_ms": round(kms, 5),
                      "algorithmic_bytes_per_launch": step_bytes},
-        "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps,
+        # per step: decode_bulk_kernel + slot_merge_kernel (every sequence of
+        # these batches spans several chunks)
+        "clocks": clocks, "e2e": e2e, "gpu_launches": 2 * args.steps,
     })
     if not args.no_prefill and wl == "llama3_decode":
         pre = run_prefill(dev, max(3, args.prefill_steps), 3, dist, peaks)
@@ -545,13 +554,123 @@ def run_longctx(args, dist, peaks, res):
                 "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                              "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
                              "traffic": profile_traffic("decode_longctx.txt"),
-                             "kernel": decode_kernel_name(torch.bfloat16, d, Hkv, H // Hkv, 1),
+                             "kernel": decode_kernel_name(torch.bfloat16, d, Hkv, H // Hkv) + " + slot_merge_kernel",
                              "kernel_ms": round(kms, 5)},
-                "clocks": clocks, "gpu_launches": args.steps * (1 if dist.world == 1 else 2)})
+                # per step: decode_bulk_kernel + slot_merge_kernel (the
+                # partials) + merge_lse_packed_kernel; NCCL's all-gather between
+                "clocks": clocks, "gpu_launches": 3 * args.steps})
     if dist.world == 1 and not args.no_cpu:
         v, thr, desc = cpu_decode_sample("longctx", args.cpu_budget)
         res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
                                "sample": desc}
+    emit(res, dist)
+
+
+def run_serving(args, dist, peaks, res):
+    """DecodeBatcher over 32 Llama-3-shaped requests; one step = one token of
+    every request through all layers, with a leave + join every 8 steps."""
+    import numpy as np
+    import torch
+
+    import bml_b200
+    dev = dist.device
+    n_req, n_layers, H, Hkv, d = 32, 32, 32, 8, 128
+    row = Hkv * d * 2
+    rng = np.random.default_rng(6 + 1000 * dist.rank)
+    lens0 = [int(x) for x in rng.integers(1024, 4097, n_req)]
+    total_steps = args.steps + args.warmup + 8
+    cap = ((max(lens0) + total_steps + 255) // 256) * 256
+    gen = torch.Generator(device=dev).manual_seed(6 + 1000 * dist.rank)
+    k_prompt = gen_normal((n_layers, 4096, Hkv, d), torch.bfloat16, dev, gen)
+    v_prompt = gen_normal((n_layers, 4096, Hkv, d), torch.bfloat16, dev, gen)
+    b = bml_b200.DecodeBatcher(n_layers, H, Hkv, d, dtype=torch.bfloat16, device=dev, rope=True)
+    next_id = [0]
+
+    def join(L):
+        b.add(next_id[0], cap, k_prompt[:, :L], v_prompt[:, :L])
+        next_id[0] += 1
+
+    for L in lens0:
+        join(L)
+    q = gen_normal((n_layers, n_req, H, d), torch.float32, dev, gen)
+    kn = gen_normal((n_layers, n_req, Hkv, d), torch.float32, dev, gen)
+    vn = gen_normal((n_layers, n_req, Hkv, d), torch.float32, dev, gen)
+    out = torch.empty(n_req, H, d, dtype=torch.float32, device=dev)
+    state = {"t": 0, "bytes": 0}
+    # per request and layer: KV read over len+1 positions, q read, out
+    # written, and the append (q read+write, k/v f32 read, k/v bf16 write)
+    per_layer_fixed = H * d * 4 * 2 + H * d * 4 * 2 + 2 * Hkv * d * 4 + 2 * row
+
+    def token():
+        if state["t"] and state["t"] % 8 == 0:
+            longest = max(b.active, key=b.length)
+            b.remove(longest)
+            join(int(rng.integers(1024, 4097)))
+        state["bytes"] += n_layers * sum(2 * (b.length(r) + 1) * row + per_layer_fixed for r in b.active)
+        for layer in range(n_layers):
+            b.step(layer, q[layer], kn[layer], vn[layer], out=out)
+        b.advance()
+        state["t"] += 1
+
+    token()
+    torch.cuda.synchronize()
+    state["bytes"] = 0
+    for _ in range(args.warmup):
+        token()
+    torch.cuda.synchronize()
+    warm_bytes = state["bytes"]
+    ms, clocks = timed_loop(token, args.steps, 0, dist, dist.local)
+    step_bytes = (state["bytes"] - warm_bytes) / args.steps
+    total = dist.sum(step_bytes)
+    gbs = total * args.steps / (ms * 1e-3) / 1e9
+    b.workspace.check()
+
+    # end to end: each token's q/k/v of every layer from pinned host memory,
+    # the last layer's attention output back to the host
+    qh, kh, vh = q.cpu().pin_memory(), kn.cpu().pin_memory(), vn.cpu().pin_memory()
+    oh = torch.empty(n_req, H, d, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream()
+
+    def token_e2e():
+        q.copy_(qh, non_blocking=True)
+        kn.copy_(kh, non_blocking=True)
+        vn.copy_(vh, non_blocking=True)
+        token()
+        oh.copy_(out, non_blocking=True)
+        stream.synchronize()
+
+    n = max(5, min(args.steps, 100))
+    for _ in range(2):
+        token_e2e()
+    dist.barrier()
+    torch.cuda.synchronize()
+    b0 = state["bytes"]
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n):
+        token_e2e()
+    e.record(stream)
+    torch.cuda.synchronize()
+    ems = dist.max(a.elapsed_time(e))
+    e2e = {"value": round(dist.sum((state["bytes"] - b0) / n) * n / (ems * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "h2d_bytes_per_step": (qh.numel() + kh.numel() + vh.numel()) * 4, "d2h_bytes_per_step": oh.numel() * 4,
+           "steps": n, "ms_per_step": round(ems / n, 4),
+           "tokens_per_s": round(dist.sum(n_req) * n / (ems * 1e-3), 1)}
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    ach = step_bytes / (ms / args.steps * 1e-3) / 1e9
+    res.update({"metric": DECODE_METRIC, "value": round(gbs, 1), "unit": "GB/s",
+                "ms_per_step": round(ms / args.steps, 5), "scaling": "weak", "dtype": "f32 (bf16 KV)",
+                "config": {"workload": "serving", "n_requests": n_req, "n_layers": n_layers, "n_heads": H,
+                           "n_kv_heads": Hkv, "head_dim": d, "kv_dtype": "bf16", "prompts": "U[1024,4096] seed 6",
+                           "churn": "longest request leaves, a new one joins, every 8 steps",
+                           "tokens_per_s": round(dist.sum(n_req) * args.steps / (ms * 1e-3), 1),
+                           "l2": "~10 GB of KV read per step vs 126 MB L2"},
+                "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                             "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
+                             "traffic": None,
+                             "kernel": "decode_bulk_kernel + slot_merge_kernel + rope_append_rows_kernel, 32 layers per step",
+                             "algorithmic_bytes_per_step": round(step_bytes)},
+                "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps * n_layers * 3})
     emit(res, dist)
 
 
@@ -606,7 +725,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="llama3_decode",
-                    choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill"])
+                    choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill", "serving"])
     ap.add_argument("--prefill-steps", type=int, default=200)
     ap.add_argument("--prefill-n", type=int, default=4, help="prefill sequences (llama3_prefill)")
     ap.add_argument("--prefill-s", type=int, default=8192, help="prefill tokens per sequence")

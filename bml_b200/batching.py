@@ -80,6 +80,8 @@ class DecodeBatcher:
         self._lens = None    # per-layer numpy views of their len fields
         self._host_lens = np.zeros(0, np.uint32)
         self._caps = np.zeros(0, np.uint32)
+        self._full = False
+        self._ws_n = -1
 
     # -- membership -------------------------------------------------------
     @property
@@ -102,8 +104,10 @@ class DecodeBatcher:
         if len(self._order) >= self.max_requests:
             raise AtCapacity(f"{len(self._order)} requests active (max {self.max_requests})")
         shape = (self.n_layers, capacity, self.n_kv, self.head_dim)
-        k = torch.zeros(shape, dtype=self.dtype, device=self.device)
-        v = torch.zeros(shape, dtype=self.dtype, device=self.device)
+        # uninitialised: a row is written (prompt copy or append) before any
+        # kernel reads it, and no kernel reads past a request's length
+        k = torch.empty(shape, dtype=self.dtype, device=self.device)
+        v = torch.empty(shape, dtype=self.dtype, device=self.device)
         n = 0
         if k_prompt is not None:
             if v_prompt is None or k_prompt.shape != v_prompt.shape:
@@ -138,6 +142,7 @@ class DecodeBatcher:
             self._lens.append(_len_view(arr, max(n, 1))[:n])
         self._host_lens = np.array([self._reqs[r].length for r in self._order], np.uint32)
         self._caps = np.array([self._reqs[r].k.shape[1] for r in self._order], np.uint32)
+        self._full = bool((self._host_lens >= self._caps).any())
 
     # -- one layer of one token -------------------------------------------
     def step(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
@@ -159,9 +164,8 @@ class DecodeBatcher:
                 tuple(k_new.shape) != (n, self.n_kv, self.head_dim) or k_new.shape != v_new.shape:
             raise ValueError(f"q {tuple(q.shape)} / k_new {tuple(k_new.shape)} do not match "
                              f"{n} requests x ({self.n_heads}|{self.n_kv}, {self.head_dim})")
-        full = np.nonzero(self._host_lens >= self._caps)[0]
-        if full.size:
-            rid = self._order[int(full[0])]
+        if self._full:
+            rid = self._order[int(np.nonzero(self._host_lens >= self._caps)[0][0])]
             raise ValueError(f"request {rid!r} is full ({self._reqs[rid].length} positions)")
         lens = self._lens[layer]
         descs = self._descs[layer]
@@ -180,7 +184,10 @@ class DecodeBatcher:
             out = torch.empty_like(q)
         else:
             _need(out, "out", torch.float32, 3)
-        ws = self.workspace.ensure(n, self.n_heads, self.head_dim)
+        if self._ws_n != n:
+            self.workspace.ensure(n, self.n_heads, self.head_dim)
+            self._ws_n = n
+        ws = self.workspace
         L.call("bml_attn_decode_batched", descs, n, self.n_heads, self.n_kv, self.head_dim,
                dtype_code(self.dtype), self.scale, _ptr(q), _ptr(out), ws.ptr, ws.nbytes, st)
         return out
@@ -190,6 +197,7 @@ class DecodeBatcher:
         for rid in self._order:
             self._reqs[rid].length += 1
         self._host_lens = self._host_lens + 1
+        self._full = bool((self._host_lens >= self._caps).any())
 
     def cache(self, rid, layer: int):
         """(K, V) views [length, n_kv, d] of request `rid`'s layer."""

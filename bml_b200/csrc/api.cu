@@ -421,44 +421,87 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
     bml::DecodeWorkspace ws;
     if (!bml::decode_workspace_carve(workspace, ws_bytes, n_seqs, n_heads, head_dim, sms, &ws))
         return fail(BML_E_INVALID, "%s: workspace of %zu bytes, need %zu", fn, ws_bytes,
-                    bml::decode_workspace_bytes(n_seqs, n_heads, head_dim, sms));
+                    bml::decode_workspace_min_bytes(n_seqs, n_heads, head_dim, sms));
 
     const float sc = resolve_scale(scale, head_dim);
     const size_t es = bml::dtype_size(dt);
     const uint32_t T = bml::decode_rows_per_tile(dt, head_dim, n_kv);
+    const uint32_t group = n_heads / n_kv;
     static thread_local bml::DecodeParams p;  // ~8 KB, kept off the stack
     // the TMA kernel carries two tensor maps per sequence in its parameters:
-    // when it is forced, launches take at most its 64 sequences (by default
-    // larger launches go to the bulk-copy kernel)
+    // when it is forced, launches take at most its 64 sequences
     const uint32_t chunk = bml::decode_family_override() == bml::kDecodeTma &&
-                                   bml::decode_tma_supported(dt, head_dim, n_kv, n_heads / n_kv)
+                                   bml::decode_tma_supported(dt, head_dim, n_kv, group)
                                ? bml::decode_tma_max_seqs()
                                : (uint32_t)bml::kMaxSeqsPerLaunch;
     for (uint32_t base = 0; base < n_seqs; base += chunk) {
         const uint32_t ns = std::min<uint32_t>(n_seqs - base, chunk);
         memset(&p, 0, offsetof(bml::DecodeParams, seqs));
+        p.n_seqs = ns;
+        p.n_kv = n_kv;
         uint64_t total = 0;
-        for (uint32_t s = 0; s < ns; ++s) total += (seqs[base + s].len + T - 1) / T;
-        if (total > 0xffffffffull) return fail(BML_E_INVALID, "%s: batch too large", fn);
-        const uint32_t tpc = (uint32_t)((total + sms - 1) / sms);
-        const int grid = (int)((total + tpc - 1) / tpc);
-        uint32_t tile = 0, slot = 0;
         for (uint32_t s = 0; s < ns; ++s) {
             const bml_seq_desc &d = seqs[base + s];
-            const uint32_t nt = (d.len + T - 1) / T;
             bml::DecodeSeq &e = p.seqs[s];
             e.k = d.k_dev;
             e.v = d.v_dev;
             e.len = d.len;
-            e.tile_begin = tile;
-            e.slot_base = slot;
-            e.n_slots = (tile + nt - 1) / tpc - tile / tpc + 1;
-            tile += nt;
-            slot += e.n_slots;
+            total += (d.len + T - 1) / T;
+        }
+        if (total > 0xffffffffull) return fail(BML_E_INVALID, "%s: batch too large", fn);
+        const bml::DecodeKernel kern = bml::decode_select(p, dt, head_dim, group);
+        int grid = 0;
+        uint32_t slot = 0, max_slots_seq = 0;
+        if (kern == bml::kKernBulk) {
+            // Dynamic schedule: chunks of C tiles, about 8 per SM, claimed at
+            // run time.  Each chunk leaves one partial slot per warp of a kv
+            // head (8 / n_kv), so C grows until the slots fit the workspace.
+            const uint32_t nph = 8u / n_kv;
+            uint64_t C = std::max<uint64_t>(4, (total + 8ull * sms - 1) / (8ull * sms));
+            // (launch_slot_merge takes at most 1024 slots a sequence)
+            auto fits = [&](uint64_t c) {
+                uint64_t n = 0;
+                for (uint32_t s = 0; s < ns; ++s) {
+                    const uint64_t k = ((p.seqs[s].len + T - 1) / T + c - 1) / c;
+                    if (k * nph > 1024) return false;
+                    n += k;
+                }
+                return n * nph <= ws.max_slots;
+            };
+            while (!fits(C)) C = C + C / 4 + 1;
+            uint32_t chunk_no = 0;
+            for (uint32_t s = 0; s < ns; ++s) {
+                bml::DecodeSeq &e = p.seqs[s];
+                const uint32_t nc = (uint32_t)(((e.len + T - 1) / T + C - 1) / C);
+                e.tile_begin = chunk_no;
+                e.slot_base = chunk_no * nph;
+                e.n_slots = nc * nph;
+                chunk_no += nc;
+                max_slots_seq = std::max(max_slots_seq, e.n_slots);
+            }
+            slot = chunk_no * nph;
+            p.chunk_tiles = (uint32_t)C;
+            p.total_chunks = chunk_no;
+            p.sched = ws.sched;
+            grid = (int)std::min<uint32_t>((uint32_t)sms, chunk_no);
+        } else {
+            // Static schedule: contiguous ranges of tpc tiles per CTA.
+            const uint32_t tpc = (uint32_t)((total + sms - 1) / sms);
+            grid = (int)((total + tpc - 1) / tpc);
+            uint32_t tile = 0;
+            for (uint32_t s = 0; s < ns; ++s) {
+                bml::DecodeSeq &e = p.seqs[s];
+                const uint32_t nt = (e.len + T - 1) / T;
+                e.tile_begin = tile;
+                e.slot_base = slot;
+                e.n_slots = (tile + nt - 1) / tpc - tile / tpc + 1;
+                tile += nt;
+                slot += e.n_slots;
+                max_slots_seq = std::max(max_slots_seq, e.n_slots);
+            }
+            p.tiles_per_cta = tpc;
         }
         if (slot > ws.max_slots) return fail(BML_E_INVALID, "%s: internal slot overflow", fn);
-        uint32_t max_slots_seq = 0;
-        for (uint32_t s = 0; s < ns; ++s) max_slots_seq = std::max(max_slots_seq, p.seqs[s].n_slots);
         p.q = q + (size_t)base * n_heads * head_dim;
         p.out = out ? out + (size_t)base * n_heads * head_dim : nullptr;
         p.part_m = pm ? pm + (size_t)base * n_heads : nullptr;
@@ -468,17 +511,16 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
         p.slot_o = ws.slot_o;
         p.counters = ws.counters;
         p.err = ws.err;
-        p.n_seqs = ns;
         p.n_heads = n_heads;
-        p.n_kv = n_kv;
         p.rows_per_tile = T;
         p.total_tiles = (uint32_t)total;
-        p.tiles_per_cta = tpc;
         p.row_bytes = (uint32_t)(n_kv * head_dim * es);
         p.qscale = (float)((double)sc * 1.4426950408889634);
         p.mode = mode;
-        p.merge_in_kernel = max_slots_seq <= bml::kInKernelMergeMaxSlots ? 1 : 0;
-        CUDA_TRY(bml::launch_decode(p, dt, head_dim, n_heads / n_kv, grid, static_cast<cudaStream_t>(stream)), fn);
+        // the bulk kernel leaves every multi-slot sequence to launch_slot_merge
+        p.merge_in_kernel = kern == bml::kKernBulk ? (max_slots_seq <= 1 ? 1 : 0)
+                                                   : (max_slots_seq <= bml::kInKernelMergeMaxSlots ? 1 : 0);
+        CUDA_TRY(bml::launch_decode(p, kern, dt, head_dim, group, grid, static_cast<cudaStream_t>(stream)), fn);
         if (!p.merge_in_kernel)
             CUDA_TRY(bml::launch_slot_merge(p, head_dim, static_cast<cudaStream_t>(stream)), fn);
     }
@@ -683,7 +725,7 @@ BML_API bml_status bml_attn_decode_batched_noalloc(const bml_seq_desc *seqs_host
     if (st != BML_OK) return st;
     if (!seqs_host || n_seqs == 0) return fail(BML_E_INVALID, "%s: no sequences", fn);
     const int dev = current_device();
-    const size_t need = bml::decode_workspace_bytes(n_seqs, n_heads, head_dim, num_sms(dev));
+    const size_t need = bml::decode_workspace_min_bytes(n_seqs, n_heads, head_dim, num_sms(dev));
     if (need > kNoAllocScratchBytes)
         return fail(BML_E_INVALID, "%s: needs %zu bytes of scratch, above the fixed %zu-byte maximum", fn, need,
                     kNoAllocScratchBytes);

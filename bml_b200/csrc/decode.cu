@@ -655,33 +655,52 @@ uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv) {
 }
 
 // Scratch layout, fixed part first so that calls of any shape agree on it:
-//   [0, 256)                  error word
+//   [0, 64)                   error word
+//   [64, 72)                  dynamic-schedule claim counter and CTA exit
+//                             ticket; each call leaves them zero
 //   [256, 256 + kTicketBytes) merge tickets: one per (sequence, kv head) of a
 //                             launch (256 sequences x 8 kv heads at most); each
 //                             call leaves them zero
-//   then partial slots for (2*seqs + SMs) split points of n_heads rows each.
+//   then partial slots of n_heads rows each: as many as the workspace holds,
+//   at least 2*seqs + SMs (the static schedule's split points); the
+//   recommended size holds 2*seqs + 8*SMs (dynamic-schedule chunks).
 // A shape-dependent ticket area would let one call read another call's
 // leftover slot values as tickets.
 constexpr size_t kTicketBytes = (size_t)kMaxSeqsPerLaunch * 8 * 4;
 
-size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, int num_sms) {
-    const size_t seqs = n_seqs < (uint32_t)kMaxSeqsPerLaunch ? n_seqs : kMaxSeqsPerLaunch;
-    const size_t slots = 2 * seqs + (size_t)num_sms;
+namespace {
+
+size_t workspace_bytes_for(size_t slots, uint32_t n_heads, uint32_t head_dim) {
     size_t b = 256 + kTicketBytes;
     b += ((slots * n_heads * 2 * 4 + 255) / 256) * 256;   // slot (m, l)
     b += slots * n_heads * head_dim * 4;                  // slot o
     return b;
 }
 
+size_t launch_seqs(uint32_t n_seqs) { return n_seqs < (uint32_t)kMaxSeqsPerLaunch ? n_seqs : kMaxSeqsPerLaunch; }
+
+}  // namespace
+
+size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, int num_sms) {
+    return workspace_bytes_for(2 * launch_seqs(n_seqs) + 8 * (size_t)num_sms, n_heads, head_dim);
+}
+
+size_t decode_workspace_min_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, int num_sms) {
+    return workspace_bytes_for(2 * launch_seqs(n_seqs) + (size_t)num_sms, n_heads, head_dim);
+}
+
 size_t decode_workspace_zero_bytes() { return 256 + kTicketBytes; }
 
 bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
                             int num_sms, DecodeWorkspace *out) {
-    if (!ws || bytes < decode_workspace_bytes(n_seqs, n_heads, head_dim, num_sms)) return false;
-    const size_t seqs = n_seqs < (uint32_t)kMaxSeqsPerLaunch ? n_seqs : kMaxSeqsPerLaunch;
-    const size_t slots = 2 * seqs + (size_t)num_sms;
+    if (!ws || bytes < decode_workspace_min_bytes(n_seqs, n_heads, head_dim, num_sms)) return false;
+    // the largest slot count whose layout fits in `bytes`
+    const size_t per_slot = (size_t)n_heads * (2 + head_dim) * 4;
+    size_t slots = (bytes - 256 - kTicketBytes - 256) / per_slot;
+    while (slots > 0 && workspace_bytes_for(slots, n_heads, head_dim) > bytes) --slots;
     uint8_t *b = static_cast<uint8_t *>(ws);
     out->err = reinterpret_cast<uint32_t *>(b);
+    out->sched = reinterpret_cast<uint32_t *>(b + 64);
     b += 256;
     out->counters = reinterpret_cast<uint32_t *>(b);
     b += kTicketBytes;
@@ -704,26 +723,29 @@ DecodeFamily decode_family_override() {
     return fam;
 }
 
-cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
-                          int grid, cudaStream_t stream) {
-    // 16-bit caches of the common shapes take the tensor-core kernels: TMA
-    // tile loads (decode_tma.cu) for launches of up to 64 sequences, whole-
-    // group bulk copies (decode_bulk.cu) for larger ones, cp.async loads
-    // (decode_mma.cu) where neither applies; everything else the CUDA-core
-    // kernel below.
+DecodeKernel decode_select(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group) {
+    // 16-bit caches of the common shapes take the tensor-core kernels: group
+    // bulk copies with the dynamic schedule (decode_bulk.cu) by default, TMA
+    // tile loads (decode_tma.cu) or cp.async loads (decode_mma.cu) where it
+    // does not apply or is overridden; everything else the CUDA-core kernel.
     const DecodeFamily fam = decode_family_override();
-    const bool tma_fits = p.n_seqs <= decode_tma_max_seqs();
-    if ((fam == kDecodeTma || (fam == kDecodeAuto && tma_fits)) && tma_fits &&
-        decode_tma_supported(dt, head_dim, p.n_kv, group)) {
-        const cudaError_t e = launch_decode_tma(p, dt, head_dim, group, grid, stream);
-        if (e != cudaErrorNotSupported) return e;
+    const bool tma_ok = p.n_seqs <= decode_tma_max_seqs() && decode_tma_supported(dt, head_dim, p.n_kv, group);
+    const bool bulk_ok = decode_bulk_supported(dt, head_dim, p.n_kv, group);
+    if (fam == kDecodeTma && tma_ok) return kKernTma;
+    if ((fam == kDecodeBulk || fam == kDecodeAuto) && bulk_ok) return kKernBulk;
+    if (fam == kDecodeAuto && tma_ok) return kKernTma;
+    if (fam != kDecodeCuda && decode_mma_supported(dt, head_dim, p.n_kv, group)) return kKernMma;
+    return kKernCuda;
+}
+
+cudaError_t launch_decode(const DecodeParams &p, DecodeKernel kern, bml_dtype dt, uint32_t head_dim,
+                          uint32_t group, int grid, cudaStream_t stream) {
+    switch (kern) {
+        case kKernTma: return launch_decode_tma(p, dt, head_dim, group, grid, stream);
+        case kKernBulk: return launch_decode_bulk(p, dt, head_dim, group, grid, stream);
+        case kKernMma: return launch_decode_mma(p, dt, head_dim, group, grid, stream);
+        case kKernCuda: break;
     }
-    if ((fam == kDecodeAuto || fam == kDecodeBulk) && decode_bulk_supported(dt, head_dim, p.n_kv, group)) {
-        const cudaError_t e = launch_decode_bulk(p, dt, head_dim, group, grid, stream);
-        if (e != cudaErrorNotSupported) return e;
-    }
-    if (fam != kDecodeCuda && decode_mma_supported(dt, head_dim, p.n_kv, group))
-        return launch_decode_mma(p, dt, head_dim, group, grid, stream);
     switch (dt) {
         case BML_F32: return launch_d<float>(p, head_dim, group, grid, stream);
         case BML_F16: return launch_d<__half>(p, head_dim, group, grid, stream);

@@ -6,13 +6,20 @@
 namespace bml {
 
 // Per-sequence entry of a decode launch (host-computed schedule).
+// Static schedule (chunk_tiles == 0): CTA b owns global tiles
+// [b*tiles_per_cta, (b+1)*tiles_per_cta); tile_begin is the sequence's first
+// global tile and its n_slots partial slots are one per CTA touching it.
+// Dynamic schedule (chunk_tiles > 0): the sequence is cut into n_slots
+// chunks of chunk_tiles tiles, global chunk indices [tile_begin, tile_begin
+// + n_slots); CTAs claim chunks at run time and chunk c leaves its partial
+// in slot c (slot_base == tile_begin).
 struct DecodeSeq {
     const void *k;        // [len][n_kv][D]
     const void *v;
     uint32_t len;         // positions attended
-    uint32_t tile_begin;  // first global tile of this sequence
+    uint32_t tile_begin;  // first global tile (static) or chunk (dynamic)
     uint32_t slot_base;   // first partial slot of this sequence
-    uint32_t n_slots;     // CTAs that touch this sequence
+    uint32_t n_slots;     // CTAs (static) or chunks (dynamic) of this sequence
 };
 
 constexpr int kMaxSeqsPerLaunch = 256;
@@ -38,20 +45,30 @@ struct DecodeParams {
     int mode;
     int merge_in_kernel;      // 1: last CTA of a sequence merges its slots;
                               // 0: slots are merged by launch_slot_merge
+    uint32_t chunk_tiles;     // dynamic schedule: tiles per chunk (0: static)
+    uint32_t total_chunks;
+    uint32_t *sched;          // dynamic schedule: [0] chunk claims, [1] CTA exit
+                              // ticket; zero between calls
     DecodeSeq seqs[kMaxSeqsPerLaunch];
 };
 
 // Scratch layout inside a caller workspace.
 struct DecodeWorkspace {
     uint32_t *err;
+    uint32_t *sched;
     uint32_t *counters;
     float *slot_ml;
     float *slot_o;
     size_t max_slots;
 };
 
+// Recommended scratch bytes (room for the dynamic schedule's chunk slots)
+// and the minimum a call accepts (the static schedule's slots); the
+// dynamic schedule sizes its chunks to the slots a workspace holds.
 size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
                               int num_sms);
+size_t decode_workspace_min_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
+                                  int num_sms);
 // Bytes at the start of a workspace that must be zero before a call
 // (error word and merge tickets).
 size_t decode_workspace_zero_bytes();
@@ -61,10 +78,16 @@ bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_
 // Rows of one tile for a (dtype, head_dim, n_kv) combination.
 uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv);
 
-// Launches one decode kernel; returns a CUDA error code.  The kernel is
-// selected from (dtype, head_dim, group); unsupported combinations return
-// cudaErrorNotSupported.
-cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim,
+enum DecodeKernel : int { kKernTma = 0, kKernBulk = 1, kKernMma = 2, kKernCuda = 3 };
+
+// The kernel a launch takes, from the shape, the family override and the
+// sequences of p (n_seqs, n_kv and seqs[].k / v / len filled in).  The
+// bulk-copy kernel runs the dynamic schedule, every other kernel the static
+// one.
+DecodeKernel decode_select(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group);
+
+// Launches the selected decode kernel; returns a CUDA error code.
+cudaError_t launch_decode(const DecodeParams &p, DecodeKernel kern, bml_dtype dt, uint32_t head_dim,
                           uint32_t group, int grid, cudaStream_t stream);
 
 // Tensor-core (mma.sync m16n8k16) variant for 16-bit caches, same
@@ -81,15 +104,15 @@ cudaError_t launch_decode_mma(const DecodeParams &p, bml_dtype dt, uint32_t head
 bool decode_tma_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
 uint32_t decode_tma_max_seqs();
 
-// Same arithmetic with each cache row brought in by one 1-D bulk copy into
-// padded shared-memory rows (decode_bulk.cu); 256 sequences a launch.
+// Same arithmetic with tiles brought in by group bulk copies into staggered
+// shared-memory rows and chunks of tiles claimed at run time (decode_bulk.cu,
+// dynamic schedule only); 256 sequences a launch.
 bool decode_bulk_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
 cudaError_t launch_decode_bulk(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                                int grid, cudaStream_t stream);
 
-// Kernel family for 16-bit caches.  By default (kDecodeAuto) a launch of at
-// most decode_tma_max_seqs() sequences takes the TMA kernel and a larger one
-// the bulk-copy kernel (one launch instead of several); BML_DECODE_KERNEL=tma,
+// Kernel family for 16-bit caches.  By default (kDecodeAuto) the bulk-copy
+// kernel with the dynamic schedule; BML_DECODE_KERNEL=tma,
 // =bulk, =mma or =cuda in the environment (read once) forces the TMA, bulk-
 // copy, cp.async warp-MMA or CUDA-core kernel -- for tests and comparisons.
 enum DecodeFamily : int { kDecodeAuto = 0, kDecodeMma = 1, kDecodeCuda = 2, kDecodeBulk = 3, kDecodeTma = 4 };
