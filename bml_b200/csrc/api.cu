@@ -453,17 +453,19 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
         int grid = 0;
         uint32_t slot = 0, max_slots_seq = 0;
         if (kern == bml::kKernBulk) {
-            // Dynamic schedule: chunks of C tiles, about 8 per SM, claimed at
-            // run time.  Each chunk leaves one partial slot per warp of a kv
-            // head (8 / n_kv), so C grows until the slots fit the workspace.
+            // Dynamic schedule: chunks of C tiles, about 6 per SM, claimed at
+            // run time (measured: 4-12 per SM within 3% on batches; fewer
+            // is better for one long sequence, where the partials' traffic
+            // and merge weigh more).  Each chunk leaves one partial slot per
+            // warp of a kv head (8 / n_kv), so C grows until the slots fit
+            // the workspace and a sequence has at most 512 of them.
             const uint32_t nph = 8u / n_kv;
-            uint64_t C = std::max<uint64_t>(4, (total + 8ull * sms - 1) / (8ull * sms));
-            // (launch_slot_merge takes at most 1024 slots a sequence)
+            uint64_t C = std::max<uint64_t>(4, (total + 6ull * sms - 1) / (6ull * sms));
             auto fits = [&](uint64_t c) {
                 uint64_t n = 0;
                 for (uint32_t s = 0; s < ns; ++s) {
                     const uint64_t k = ((p.seqs[s].len + T - 1) / T + c - 1) / c;
-                    if (k * nph > 1024) return false;
+                    if (k * nph > 512) return false;
                     n += k;
                 }
                 return n * nph <= ws.max_slots;

@@ -585,13 +585,20 @@ __global__ void merge_lse_packed_kernel(const float *__restrict__ parts, uint32_
     out[idx] = O / L;
 }
 
-// One CTA per (sequence, head) row of a sequence with several slots: the
-// slot weights 2^(m_i - M) l_i are computed once per slot in shared memory,
-// then each thread accumulates one output element over the slots in order.
-__global__ void __launch_bounds__(128) slot_merge_kernel(const __grid_constant__ DecodeParams p,
+// Merge of a sequence's slots, one CTA per (sequence, head, block of
+// 32 * VEC output dims; a row is split into head_dim / (32 * VEC) blocks).
+// The slot weights 2^(m_i - M) l_i are computed once per slot in shared
+// memory (by every CTA of the row: n_slots x 2 floats); then warp w sums
+// slots w, w+8, w+16, ... for the CTA's dims (one 128*VEC-byte load per slot
+// and warp, many in flight), and the 8 warp sums are added in warp order --
+// a fixed order, so results do not vary between runs.  Few rows (one long
+// context) take VEC = 1 for more CTAs; many rows take whole rows per CTA.
+template <int VEC>
+__global__ void __launch_bounds__(256) slot_merge_kernel(const __grid_constant__ DecodeParams p,
                                                          uint32_t head_dim) {
     __shared__ float w[1024];
-    __shared__ float red[4];
+    __shared__ float red[8];
+    __shared__ float part[8][32 * VEC];
     const uint32_t s = blockIdx.x / p.n_heads, qh = blockIdx.x % p.n_heads;
     const DecodeSeq &sq = p.seqs[s];
     if (sq.n_slots <= 1) return;  // written directly by the decode kernel
@@ -604,7 +611,9 @@ __global__ void __launch_bounds__(128) slot_merge_kernel(const __grid_constant__
     for (int m = 16; m > 0; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
     if (lane == 0) red[warp] = mx;
     __syncthreads();
-    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float M = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) M = fmaxf(M, red[i]);
     __syncthreads();
     float lsum = 0.f;
     for (uint32_t i = tid; i < n; i += blockDim.x) {
@@ -617,15 +626,42 @@ __global__ void __launch_bounds__(128) slot_merge_kernel(const __grid_constant__
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, m);
     if (lane == 0) red[warp] = lsum;
-    __syncthreads();
-    const float L = (red[0] + red[1]) + (red[2] + red[3]);
-    const size_t row = (size_t)s * p.n_heads + qh;
-    for (uint32_t d = tid; d < head_dim; d += blockDim.x) {
-        float O = 0.f;
-        const float *src = p.slot_o + ((size_t)sq.slot_base * p.n_heads + qh) * head_dim + d;
-        const size_t stride = (size_t)p.n_heads * head_dim;
+    __syncthreads();  // also publishes w[]
+    float L = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) L += red[i];
+    const uint32_t d0 = (blockIdx.y * 32 + lane) * VEC;
+    const size_t stride = (size_t)p.n_heads * head_dim;
+    const float *src = p.slot_o + ((size_t)sq.slot_base * p.n_heads + qh) * head_dim + d0;
+    float acc[VEC];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
 #pragma unroll 8
-        for (uint32_t i = 0; i < n; ++i) O += __ldcg(src + i * stride) * w[i];
+    for (uint32_t i = warp; i < n; i += 8) {
+        const float wi = w[i];
+        if constexpr (VEC == 4) {
+            const float4 x = __ldcg(reinterpret_cast<const float4 *>(src + i * stride));
+            acc[0] += x.x * wi;
+            acc[1] += x.y * wi;
+            acc[2] += x.z * wi;
+            acc[3] += x.w * wi;
+        } else if constexpr (VEC == 2) {
+            const float2 x = __ldcg(reinterpret_cast<const float2 *>(src + i * stride));
+            acc[0] += x.x * wi;
+            acc[1] += x.y * wi;
+        } else {
+            acc[0] += __ldcg(src + i * stride) * wi;
+        }
+    }
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) part[warp][lane * VEC + v] = acc[v];
+    __syncthreads();
+    const size_t row = (size_t)s * p.n_heads + qh;
+    for (uint32_t e = tid; e < 32u * VEC; e += blockDim.x) {
+        float O = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) O += part[i][e];
+        const uint32_t d = blockIdx.y * 32 * VEC + e;
         if (p.mode == kModeFinal) {
             p.out[row * head_dim + d] = O / L;
         } else {
@@ -643,7 +679,19 @@ __global__ void __launch_bounds__(128) slot_merge_kernel(const __grid_constant__
 cudaError_t launch_slot_merge(const DecodeParams &p, uint32_t head_dim, cudaStream_t stream) {
     const unsigned blocks = p.n_seqs * p.n_heads;
     if (blocks == 0) return cudaSuccess;
-    slot_merge_kernel<<<blocks, 128, 0, stream>>>(p, head_dim);
+    if (head_dim % 32 != 0 || head_dim > 128) return cudaErrorInvalidValue;
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (blocks < 2u * (unsigned)sms || head_dim == 32) {
+        slot_merge_kernel<1><<<dim3(blocks, head_dim / 32), 256, 0, stream>>>(p, head_dim);
+    } else if (head_dim == 64) {
+        slot_merge_kernel<2><<<dim3(blocks, 1), 256, 0, stream>>>(p, head_dim);
+    } else if (head_dim == 128) {
+        slot_merge_kernel<4><<<dim3(blocks, 1), 256, 0, stream>>>(p, head_dim);
+    } else {
+        slot_merge_kernel<1><<<dim3(blocks, head_dim / 32), 256, 0, stream>>>(p, head_dim);
+    }
     return cudaGetLastError();
 }
 
