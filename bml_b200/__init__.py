@@ -13,9 +13,12 @@ package is its host-side mirror of the reference interface:
                      KV-split flash decoding (no reference counterpart)
   DecodeBatcher      continuous batching of decode steps, the batched form
                      of crates/api/src/main.rs:266-354's one-request loop
+  read_tensor_f32 / WeightTensor.matmul_f64
+                     gguf_compiler.rs:351-470 and :1239-1255 on the device
 """
 from ._lib import BmlError, BmlInvalid, BmlUnsupported, last_error  # noqa: F401
 from .attention import (SeqBatch, Workspace, decode_batched, decode_partial,  # noqa: F401
                         merge_lse, merge_lse_packed, prefill, softmax_f32)
 from .kv_cache import HashConsedKV  # noqa: F401
 from .batching import AtCapacity, DecodeBatcher, MAX_PENDING_REQUESTS  # noqa: F401
+from .weights import WeightTensor, matmul_f64, read_tensor_f32  # noqa: F401

@@ -47,6 +47,7 @@ class bml_seq_desc(C.Structure):
 
 # name -> (restype, argtypes); mirrors include/bml_attn.h one to one.
 _vp, _u32, _i32, _st, _sz = C.c_void_p, C.c_uint32, C.c_int32, C.c_int32, C.c_size_t
+GGUF_F32, GGUF_F16, GGUF_Q4_0, GGUF_Q8_0 = 0, 1, 2, 8  # include/bml_weights.h
 SIGNATURES = {
     "bml_last_error": (C.c_char_p, []),
     "bml_version": (C.c_char_p, []),
@@ -81,6 +82,10 @@ SIGNATURES = {
     "bml_attn_prefill": (_st, [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, C.c_int, C.c_float,
                                C.c_int, _vp, C.c_int, _vp]),
     "bml_softmax_f32": (_st, [_vp, _u32, _u32, _vp, _vp]),
+    # include/bml_weights.h
+    "bml_read_tensor_f32": (_st, [_vp, C.c_uint64, _i32, C.c_uint64, _vp, C.POINTER(C.c_uint64), _vp]),
+    "bml_matmul_workspace_size": (_st, [C.c_uint64, C.POINTER(_sz)]),
+    "bml_matmul_f64": (_st, [_vp, C.c_uint64, _i32, C.c_uint64, C.c_uint64, _vp, C.c_uint64, _vp, _vp, _sz, _vp]),
     "bml_diag_exp2": (_st, [_vp, _u32, C.c_int, _vp, _vp]),
     "bml_attn_workspace_check": (_st, [_vp, _sz, _vp]),
 }

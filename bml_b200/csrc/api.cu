@@ -18,7 +18,9 @@
 #include <vector>
 
 #include "../../include/bml_attn.h"
+#include "../../include/bml_weights.h"
 #include "decode.cuh"
+#include "gemv.cuh"
 #include "kv_ops.cuh"
 #include "prefill.cuh"
 
@@ -740,4 +742,67 @@ BML_API bml_status bml_attn_decode_batched_noalloc(const bml_seq_desc *seqs_host
              fn);
     return decode_impl(seqs_host, n_seqs, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev, nullptr,
                        nullptr, nullptr, scratch, kNoAllocScratchBytes, stream, bml::kModeFinal, fn);
+}
+
+// ---------------------------------------------------------------------------
+// Weight path: read_tensor_f32 and matmul_f64 (gguf_compiler.rs:351-470,
+// :1239-1255)
+// ---------------------------------------------------------------------------
+namespace {
+
+bool gguf_type_read(int32_t t) {
+    return t == BML_GGUF_F32 || t == BML_GGUF_F16 || t == BML_GGUF_Q4_0 || t == BML_GGUF_Q8_0;
+}
+
+bool aligned_to(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+}  // namespace
+
+BML_API bml_status bml_read_tensor_f32(const void *data_dev, uint64_t data_len, int32_t gguf_type, uint64_t n_elems,
+                                       float *out_dev, uint64_t *n_values, void *stream) {
+    const char *fn = "bml_read_tensor_f32";
+    if (!gguf_type_read(gguf_type))
+        return fail(BML_E_UNSUPPORTED, "%s: GGUF type %d (the reference reads F32, F16, Q4_0, Q8_0)", fn, gguf_type);
+    if (!n_values) return fail(BML_E_INVALID, "%s: null n_values", fn);
+    const uint64_t n = bml::gguf_values_read(gguf_type, data_len, n_elems);
+    if (n && (!data_dev || !out_dev)) return fail(BML_E_INVALID, "%s: null argument", fn);
+    if (n && (!aligned_to(data_dev, gguf_type == BML_GGUF_F32 ? 4 : 2) || !aligned_to(out_dev, 16)))
+        return fail(BML_E_INVALID, "%s: data must be %d-byte and out 16-byte aligned", fn,
+                    gguf_type == BML_GGUF_F32 ? 4 : 2);
+    CUDA_TRY(bml::read_tensor_f32(data_dev, data_len, gguf_type, n_elems, out_dev, static_cast<cudaStream_t>(stream)),
+             fn);
+    *n_values = n;
+    return ok();
+}
+
+BML_API bml_status bml_matmul_workspace_size(uint64_t n_out, size_t *bytes) {
+    if (!bytes) return fail(BML_E_INVALID, "bml_matmul_workspace_size: null output");
+    *bytes = bml::gemv_workspace_bytes(n_out);
+    return ok();
+}
+
+BML_API bml_status bml_matmul_f64(const void *w_dev, uint64_t data_len, int32_t gguf_type, uint64_t n_in,
+                                  uint64_t n_out, const double *x_dev, uint64_t x_len, double *y_dev, void *workspace,
+                                  size_t ws_bytes, void *stream) {
+    const char *fn = "bml_matmul_f64";
+    if (!gguf_type_read(gguf_type))
+        return fail(BML_E_UNSUPPORTED, "%s: GGUF type %d (the reference reads F32, F16, Q4_0, Q8_0)", fn, gguf_type);
+    if (n_out == 0) return ok();
+    if (!y_dev || (x_len && (!w_dev || !x_dev))) return fail(BML_E_INVALID, "%s: null argument", fn);
+    if ((gguf_type == BML_GGUF_Q4_0 || gguf_type == BML_GGUF_Q8_0) && n_out % 32 != 0)
+        return fail(BML_E_UNSUPPORTED, "%s: quantized tensors need n_out %% 32 == 0 (n_out %llu)", fn,
+                    (unsigned long long)n_out);
+    const uintptr_t wa = gguf_type == BML_GGUF_F32 ? 16 : gguf_type == BML_GGUF_F16 ? 16 : 2;
+    if ((w_dev && !aligned_to(w_dev, wa)) || !aligned_to(y_dev, 8) || (x_dev && !aligned_to(x_dev, 8)))
+        return fail(BML_E_INVALID, "%s: W must be %u-byte aligned, x and y 8-byte aligned", fn, (unsigned)wa);
+    if (n_in > (1ull << 40) || n_out > (1ull << 40)) return fail(BML_E_INVALID, "%s: dimensions too large", fn);
+    const int sms = num_sms(current_device());
+    const bml::GemvPlan pl = bml::gemv_plan(n_in, n_out, x_len, sms);
+    if (pl.ranges > 1 && (!workspace || ws_bytes < (size_t)pl.ranges * n_out * sizeof(double)))
+        return fail(BML_E_INVALID, "%s: workspace of %zu bytes, need %zu", fn, ws_bytes,
+                    bml::gemv_workspace_bytes(n_out));
+    CUDA_TRY(bml::gemv(w_dev, data_len, gguf_type, n_in, n_out, x_dev, x_len, y_dev, static_cast<double *>(workspace),
+                       sms, static_cast<cudaStream_t>(stream)),
+             fn);
+    return ok();
 }

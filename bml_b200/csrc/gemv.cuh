@@ -1,0 +1,35 @@
+// gemv.cuh -- launch interface of the weight-path kernels (gemv.cu).
+#pragma once
+
+#include "common.cuh"
+
+namespace bml {
+
+// GGUF tensor type ids the reference reads as f32 (crates/parser/src/gguf.rs:36-43).
+constexpr int kGgufF32 = 0, kGgufF16 = 1, kGgufQ4_0 = 2, kGgufQ8_0 = 8;
+
+// Values read_tensor_f32 returns for a tensor of n_elems elements whose data
+// is data_len bytes (0 for a type it does not read).
+uint64_t gguf_values_read(int gguf_type, uint64_t data_len, uint64_t n_elems);
+// Whole quantized blocks that decode (the rest of n_elems is zero).
+uint64_t gguf_blocks_ok(int gguf_type, uint64_t data_len, uint64_t n_elems);
+
+cudaError_t read_tensor_f32(const void *data, uint64_t data_len, int gguf_type, uint64_t n_elems, float *out,
+                            cudaStream_t st);
+
+struct GemvPlan {
+    uint64_t rows;            // min(x_len, n_in)
+    uint64_t col_tiles;       // 256-column tiles
+    uint64_t rows_per_range;
+    uint32_t ranges;          // row ranges summed by gemv_reduce_kernel
+};
+GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms);
+// Scratch for the row-range partials: at most 32 ranges of n_out doubles.
+size_t gemv_workspace_bytes(uint64_t n_out);
+
+// y[j] = sum_i x[i] * W[i*n_out + j] over the tensor's values (see gemv.cu).
+// Quantized types need n_out % 32 == 0 (cudaErrorNotSupported otherwise).
+cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in, uint64_t n_out, const double *x,
+                 uint64_t x_len, double *y, double *partial, int num_sms, cudaStream_t st);
+
+}  // namespace bml

@@ -507,3 +507,93 @@ int orc_num_threads(void) {
     return 1;
 #endif
 }
+
+/* ------------------------------------------------------------------------ */
+/* Weight path: read_tensor_f32 and matmul_f64                              */
+/* (gguf_compiler.rs:351-470, :1239-1255)                                   */
+/* ------------------------------------------------------------------------ */
+
+/* f16_to_f32 (gguf_compiler.rs:373-403): sign, 5-bit exponent, 10-bit
+ * mantissa; subnormals mant * 2^-24, exponent 31 -> inf / NaN, otherwise
+ * (1 + mant/1024) * 2^(exp-15), all exact in f32. */
+float orc_gguf_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (h >> 15) & 1u, ex = (h >> 10) & 0x1Fu, mant = h & 0x3FFu;
+    float val;
+    if (ex == 0) {
+        if (mant == 0) return sign ? -0.0f : 0.0f;
+        val = (float)mant * ldexpf(1.0f, -24);
+    } else if (ex == 0x1F) {
+        if (mant == 0) return sign ? -INFINITY : INFINITY;
+        return NAN;
+    } else {
+        val = (1.0f + (float)mant / 1024.0f) * ldexpf(1.0f, (int)ex - 15);
+    }
+    return sign ? -val : val;
+}
+
+/* GGUF tensor types the reference reads as f32 (read_tensor_f32). */
+enum { ORC_GGUF_F32 = 0, ORC_GGUF_F16 = 1, ORC_GGUF_Q4_0 = 2, ORC_GGUF_Q8_0 = 8 };
+
+/* read_tensor_f32 (gguf_compiler.rs:351-369) for n_elems elements of a
+ * tensor whose data is `data` (data_len bytes).  F32 / F16: one value per
+ * 4 / 2 bytes (chunks_exact: a trailing partial chunk is dropped, so the
+ * output has data_len / 4 or / 2 values).  Q4_0 (dequantize_q4_0,
+ * :405-438): blocks of 18 bytes, an f16 scale then 16 bytes; byte i gives
+ * elements 2i (low nibble) and 2i+1 (high nibble), value (q - 8) * scale.
+ * Q8_0 (dequantize_q8_0, :440-470): blocks of 34 bytes, an f16 scale then
+ * 32 int8, value q * scale.  Quantized types decode n_elems / 32 whole
+ * blocks, stop at the first block that does not fit in data_len, and pad
+ * with zeros up to n_elems.  Returns the number of values written, or -1
+ * for a type the reference does not read. */
+int64_t orc_read_tensor_f32(const uint8_t *data, uint64_t data_len, int type, uint64_t n_elems, float *out) {
+    if (type == ORC_GGUF_F32) {
+        const uint64_t n = data_len / 4;
+        for (uint64_t i = 0; i < n; ++i) memcpy(&out[i], data + 4 * i, 4);
+        return (int64_t)n;
+    }
+    if (type == ORC_GGUF_F16) {
+        const uint64_t n = data_len / 2;
+        for (uint64_t i = 0; i < n; ++i) {
+            const uint16_t h = (uint16_t)(data[2 * i] | (data[2 * i + 1] << 8));
+            out[i] = orc_gguf_f16_to_f32(h);
+        }
+        return (int64_t)n;
+    }
+    if (type != ORC_GGUF_Q4_0 && type != ORC_GGUF_Q8_0) return -1;
+    const uint64_t block_bytes = type == ORC_GGUF_Q4_0 ? 18 : 34;
+    const uint64_t n_blocks = n_elems / 32;
+    uint64_t w = 0;
+    for (uint64_t b = 0; b < n_blocks; ++b) {
+        const uint64_t off = b * block_bytes;
+        if (off + block_bytes > data_len) break;
+        const float scale = orc_gguf_f16_to_f32((uint16_t)(data[off] | (data[off + 1] << 8)));
+        if (type == ORC_GGUF_Q4_0) {
+            for (int i = 0; i < 16; ++i) {
+                const uint8_t byte = data[off + 2 + i];
+                out[w++] = (float)((int)(byte & 0x0F) - 8) * scale;
+                out[w++] = (float)((int)((byte >> 4) & 0x0F) - 8) * scale;
+            }
+        } else {
+            for (int i = 0; i < 32; ++i) out[w++] = (float)(int8_t)data[off + 2 + i] * scale;
+        }
+    }
+    while (w < n_elems) out[w++] = 0.0f;
+    return (int64_t)w;
+}
+
+/* matmul_f64 (gguf_compiler.rs:1239-1255): y[j] = sum over i < min(x_len,
+ * n_in) of x[i] * W[i*n_out + j], with W the tensor's f32 values in file
+ * order (w_len of them; terms past the end are skipped, as the reference
+ * skips indices past its pool), accumulated in f64 in order of i. */
+void orc_matmul_f64(const float *W, uint64_t w_len, uint64_t n_in, uint64_t n_out, const double *x, uint64_t x_len,
+                    double *y) {
+    const uint64_t rows = x_len < n_in ? x_len : n_in;
+    for (uint64_t j = 0; j < n_out; ++j) {
+        double dot = 0.0;
+        for (uint64_t i = 0; i < rows; ++i) {
+            const uint64_t idx = i * n_out + j;
+            if (idx < w_len) dot += x[i] * (double)W[idx];
+        }
+        y[j] = dot;
+    }
+}

@@ -20,6 +20,8 @@ _lib = None
 
 F32, F16, BF16 = 0, 1, 2
 K, V = 0, 1
+# GGUF tensor type ids read by read_tensor_f32 (crates/parser/src/gguf.rs:36-43)
+GGUF_F32, GGUF_F16, GGUF_Q4_0, GGUF_Q8_0 = 0, 1, 2, 8
 
 
 def build(force: bool = False) -> str:
@@ -74,6 +76,11 @@ def lib():
             L.orc_attn_decode_literal.argtypes = [vp, vp, vp, u32, u32, u32, u32, u32, u32,
                                                   u32, f64p]
             L.orc_num_threads.restype = i32
+            L.orc_gguf_f16_to_f32.restype = C.c_float
+            L.orc_gguf_f16_to_f32.argtypes = [C.c_uint16]
+            L.orc_read_tensor_f32.restype = C.c_int64
+            L.orc_read_tensor_f32.argtypes = [vp, C.c_uint64, i32, C.c_uint64, vp]
+            L.orc_matmul_f64.argtypes = [vp, C.c_uint64, C.c_uint64, C.c_uint64, vp, C.c_uint64, vp]
             _lib = L
     return _lib
 
@@ -280,3 +287,30 @@ def attn_decode_literal(q, k, v, pos, heads=None) -> np.ndarray:
 
 def num_threads() -> int:
     return int(lib().orc_num_threads())
+
+
+def f16_to_f32(h: int) -> float:
+    """gguf_compiler.rs:373-403."""
+    return float(lib().orc_gguf_f16_to_f32(h))
+
+
+def read_tensor_f32(data, gguf_type: int, n_elems: int) -> np.ndarray:
+    """read_tensor_f32 (gguf_compiler.rs:351-369) with dequantize_q4_0 /
+    dequantize_q8_0 (:405-470): the tensor's bytes -> its f32 values."""
+    buf = np.ascontiguousarray(np.frombuffer(bytes(data), dtype=np.uint8))
+    cap = max(int(n_elems), buf.size // 2 + 1)
+    out = np.zeros(cap, np.float32)
+    n = lib().orc_read_tensor_f32(_ptr(buf) if buf.size else None, buf.size, gguf_type, n_elems, _ptr(out))
+    if n < 0:
+        raise ValueError(f"GGUF type {gguf_type} is not read by the reference")
+    return out[:n]
+
+
+def matmul_f64(w: np.ndarray, n_in: int, n_out: int, x: np.ndarray) -> np.ndarray:
+    """matmul_f64 (gguf_compiler.rs:1239-1255): y = x . W, W [n_in, n_out]
+    indexed i*n_out + j over the tensor's f32 values, f64 accumulation."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    y = np.empty(n_out, np.float64)
+    lib().orc_matmul_f64(_ptr(w), w.size, n_in, n_out, _ptr(x), x.size, _ptr(y))
+    return y

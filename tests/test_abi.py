@@ -1,6 +1,6 @@
-"""The C ABI: the library loads, exports exactly what include/bml_attn.h
-declares, and rejects bad arguments on the host (no GPU needed: nothing is
-launched before validation passes)."""
+"""The C ABI: the library loads, exports exactly what include/*.h
+(bml_attn.h, bml_weights.h) declares, and rejects bad arguments on the host
+(no GPU needed: nothing is launched before validation passes)."""
 import ctypes as C
 import os
 import re
@@ -9,13 +9,15 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "bml_attn.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("bml_attn.h", "bml_weights.h")]
 
 
 def declared_functions():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(bml_[a-z0-9_]+)\s*\(", text)))
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names |= set(re.findall(r"\b(bml_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
 
 
 @pytest.fixture(scope="module")
@@ -94,3 +96,16 @@ def test_python_errors_are_typed(L):
     import bml_b200
     with pytest.raises(bml_b200.BmlInvalid):
         L.call("bml_attn_merge_lse", 16, 16, 16, 0, 4, 64, 16, None)
+
+
+def test_weight_path_rejects_on_host(L):
+    lib = L.lib()
+    n = C.c_uint64()
+    # a GGUF type the reference does not read (Q4_K)
+    assert lib.bml_read_tensor_f32(16, 144, 12, 256, 16, C.byref(n), None) == L.BML_E_UNSUPPORTED
+    # quantized tensor with n_out not a multiple of 32
+    assert lib.bml_matmul_f64(16, 18 * 8, L.GGUF_Q4_0, 16, 16, 16, 16, 16, None, 0, None) == L.BML_E_UNSUPPORTED
+    # misaligned F32 weights
+    assert lib.bml_matmul_f64(18, 64, L.GGUF_F32, 4, 4, 16, 4, 16, None, 0, None) == L.BML_E_INVALID
+    size = C.c_size_t()
+    assert lib.bml_matmul_workspace_size(4096, C.byref(size)) == L.BML_OK and size.value == 32 * 4096 * 8
