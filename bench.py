@@ -19,6 +19,13 @@ is already resident in HBM.  Workloads (--workload):
                            NCCL and merged ("strong").
   llama3_prefill           causal prefill 4 x 8192, 32/8 heads, d=128,
                            bf16 operands (TFLOP/s of 4*d*H*causal pairs).
+  gemv                     the projections of Llama-3-8B layers (q, k, v, o
+                           4096x4096/1024; gate, up 4096x14336; down
+                           14336x4096) as Q4_0 tensors read in place by
+                           matmul_f64 (x . W, the reference's indexing); a
+                           step is one layer's 7 projections, cycling over 4
+                           layers of distinct weights (490 MB > L2).  Metric:
+                           HBM GB/s of stored weight bytes + x/y ("weak").
   serving                  continuous batching (DecodeBatcher): 32 requests
                            of Llama-3-8B shape (32 layers, 32/8 heads,
                            d=128, bf16 KV), prompts U[1024,4096]; a step is
@@ -431,6 +438,8 @@ def run_b200(args):
         return run_longctx(args, dist, peaks, res)
     elif wl == "serving":
         return run_serving(args, dist, peaks, res)
+    elif wl == "gemv":
+        return run_gemv(args, dist, peaks, res)
     else:
         raise SystemExit(f"unknown workload {wl}")
 
@@ -563,6 +572,160 @@ def run_longctx(args, dist, peaks, res):
         v, thr, desc = cpu_decode_sample("longctx", args.cpu_budget)
         res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
                                "sample": desc}
+    emit(res, dist)
+
+
+# Llama-3-8B projections: (name, n_in, n_out) in the reference's (dims[0],
+# dims[1]) terms
+GEMV_LAYER = [("attn_q", 4096, 4096), ("attn_k", 4096, 1024), ("attn_v", 4096, 1024), ("attn_output", 4096, 4096),
+              ("ffn_gate", 4096, 14336), ("ffn_up", 4096, 14336), ("ffn_down", 14336, 4096)]
+
+
+def q4_0_bytes(n_elems: int, gen, dev):
+    """Random Q4_0 tensor bytes on the device: N(0, 0.02) f16 scales, random
+    nibbles."""
+    import torch
+    nb = n_elems // 32
+    raw = torch.randint(0, 256, (nb, 18), dtype=torch.uint8, device=dev, generator=gen)
+    sc = (torch.randn(nb, device=dev, generator=gen) * 0.02).to(torch.float16).view(torch.int16)
+    raw[:, 0] = (sc & 0xFF).to(torch.uint8)
+    raw[:, 1] = ((sc >> 8) & 0xFF).to(torch.uint8)
+    return raw.reshape(-1)
+
+
+def cpu_gemv_sample(budget_s: float):
+    """The oracle's matmul_f64 over the dequantised f32 values of the
+    attn_q tensor (the reference's arithmetic and loop order, one thread)."""
+    import numpy as np
+
+    import oracle
+    rng = np.random.default_rng(7)
+    n_in, n_out = 4096, 4096
+    nb = n_in * n_out // 32
+    raw = rng.integers(0, 256, (nb, 18), dtype=np.uint8)
+    sc = (rng.standard_normal(nb) * 0.02).astype(np.float16).view(np.uint16)
+    raw[:, 0], raw[:, 1] = sc & 0xFF, sc >> 8
+    w = oracle.read_tensor_f32(raw.tobytes(), oracle.GGUF_Q4_0, n_in * n_out)
+    x = rng.standard_normal(n_in)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.matmul_f64(w, n_in, n_out, x)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    nbytes = nb * 18 + (n_in + n_out) * 8
+    return nbytes / dt / 1e9, 1, f"attn_q 4096x4096 Q4_0 (f32 values, 1 thread), {reps} passes, {dt * 1e3:.1f} ms/pass"
+
+
+def run_gemv(args, dist, peaks, res):
+    import torch
+
+    import bml_b200
+    dev = dist.device
+    gen = torch.Generator(device=dev).manual_seed(8 + 1000 * dist.rank)
+    n_layers = 4
+    layers = [[bml_b200.WeightTensor(q4_0_bytes(a * b, gen, dev), bml_b200.weights.GGUF_Q4_0, [a, b])
+               for _, a, b in GEMV_LAYER] for _ in range(n_layers)]
+    xs = {a: gen_normal((a,), torch.float64, dev, gen) for _, a, _ in GEMV_LAYER}
+    ys = [torch.empty(b, dtype=torch.float64, device=dev) for _, _, b in GEMV_LAYER]
+    state = {"t": 0}
+
+    def step():
+        ws = layers[state["t"] % n_layers]
+        state["t"] += 1
+        for w, y in zip(ws, ys):
+            w.matmul_f64(xs[w.n_in], out=y)
+
+    # A layer's projections are a handful of ~5-30 us kernels, shorter than
+    # the host time of launching them one by one from Python, so a step
+    # replays a CUDA graph of the layer's launches (one graph per layer of
+    # weights), as a model's decode loop would.
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    graphs = []
+    cap = torch.cuda.Stream(device=dev)
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        for li in range(n_layers):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for w, y in zip(layers[li], ys):
+                    w.matmul_f64(xs[w.n_in], out=y)
+            graphs.append(g)
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
+
+    def step_graph():
+        graphs[state["t"] % n_layers].replay()
+        state["t"] += 1
+
+    ms, clocks = timed_loop(step_graph, args.steps, args.warmup, dist, dist.local)
+    step_bytes = sum(w.nbytes + (w.n_in + w.n_out) * 8 for w in layers[0])
+    total = dist.sum(step_bytes)
+    gbs = total * args.steps / (ms * 1e-3) / 1e9
+    # the largest projection alone: a graph of 16 launch pairs (gemv + range
+    # reduce) cycling over the 4 layers' copies so that each streams from HBM
+    bigs = [layers[i][5] for i in range(n_layers)]
+    kg = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(kg, stream=cap):
+            for i in range(16):
+                bigs[i % n_layers].matmul_f64(xs[4096], out=ys[5])
+    torch.cuda.synchronize()
+    kg.replay()
+    torch.cuda.synchronize()
+    kms = kernel_ms(kg.replay, reps=10) / 16
+    big_bytes = bigs[0].nbytes + (bigs[0].n_in + bigs[0].n_out) * 8
+    ach = big_bytes / (kms * 1e-3) / 1e9
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+
+    # end to end through the public API, launched from Python one call at a
+    # time (no graph): x from pinned host memory each step, the last y back
+    xh = {a: t.cpu().pin_memory() for a, t in xs.items()}
+    yh = torch.empty(GEMV_LAYER[-1][2], dtype=torch.float64).pin_memory()
+    stream = torch.cuda.current_stream()
+
+    def step_e2e():
+        for a in xs:
+            xs[a].copy_(xh[a], non_blocking=True)
+        step()
+        yh.copy_(ys[-1], non_blocking=True)
+        stream.synchronize()
+
+    n = max(10, min(args.steps, 200))
+    for _ in range(3):
+        step_e2e()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(n):
+        step_e2e()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ems = dist.max(a.elapsed_time(b))
+    e2e = {"value": round(total * n / (ems * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "h2d_bytes_per_step": sum(t.numel() * 8 for t in xh.values()), "d2h_bytes_per_step": yh.numel() * 8,
+           "steps": n, "ms_per_step": round(ems / n, 5)}
+    res.update({"metric": "Q4_0 projection (matmul_f64) HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
+                "ms_per_step": round(ms / args.steps, 5), "scaling": "weak", "dtype": "f32 terms, f64 sums (Q4_0 W)",
+                "config": {"workload": "gemv", "model": "Llama-3-8B projections", "layers_cycled": n_layers,
+                           "tensors": [f"{nm} {a}x{b}" for nm, a, b in GEMV_LAYER], "quant": "Q4_0",
+                           "l2": "4 layers of distinct weights, 490 MB cycled > 126 MB L2"},
+                "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                             "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
+                             "traffic": None,
+                             "kernel": "gemv_staged_kernel<Q4_0> + gemv_reduce_kernel (ffn_up 4096x14336)",
+                             "kernel_ms": round(kms, 5), "algorithmic_bytes_per_launch": big_bytes},
+                "timing": "device time of CUDA-graph replays of each layer's launches",
+                "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps * 2 * len(GEMV_LAYER)})
+    del graphs, kg
+    if dist.world == 1 and not args.no_cpu:
+        v, thr, desc = cpu_gemv_sample(args.cpu_budget)
+        res["cpu_baseline"] = {"value": round(v, 4), "unit": "GB/s", "cores": thr, "kind": "port", "sample": desc}
     emit(res, dist)
 
 
@@ -725,7 +888,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="llama3_decode",
-                    choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill", "serving"])
+                    choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill", "serving", "gemv"])
     ap.add_argument("--prefill-steps", type=int, default=200)
     ap.add_argument("--prefill-n", type=int, default=4, help="prefill sequences (llama3_prefill)")
     ap.add_argument("--prefill-s", type=int, default=8192, help="prefill tokens per sequence")

@@ -797,7 +797,8 @@ BML_API bml_status bml_matmul_f64(const void *w_dev, uint64_t data_len, int32_t 
         return fail(BML_E_INVALID, "%s: W must be %u-byte aligned, x and y 8-byte aligned", fn, (unsigned)wa);
     if (n_in > (1ull << 40) || n_out > (1ull << 40)) return fail(BML_E_INVALID, "%s: dimensions too large", fn);
     const int sms = num_sms(current_device());
-    const bml::GemvPlan pl = bml::gemv_plan(n_in, n_out, x_len, sms);
+    const bml::GemvPlan pl =
+        bml::gemv_plan(n_in, n_out, x_len, sms, bml::gemv_staged_ok(w_dev, data_len, gguf_type, n_in, n_out));
     if (pl.ranges > 1 && (!workspace || ws_bytes < (size_t)pl.ranges * n_out * sizeof(double)))
         return fail(BML_E_INVALID, "%s: workspace of %zu bytes, need %zu", fn, ws_bytes,
                     bml::gemv_workspace_bytes(n_out));

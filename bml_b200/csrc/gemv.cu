@@ -40,8 +40,11 @@ constexpr int kRowPhases = kGemvThreads / kColBlocks;  // 32
 
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
-// Exact small integers as floats: 2^23 + u has u in its low mantissa bits.
-__device__ __forceinline__ float magic_u(uint32_t u) { return __uint_as_float(0x4B000000u | u) - 8388608.0f; }
+// Exact small integers as floats: 2^23 + u has u in its low mantissa bits,
+// so (2^23 + u) - (2^23 + off) = u - off exactly (u < 2^23), in one FADD.
+__device__ __forceinline__ float magic_u(uint32_t u, float off) {
+    return __uint_as_float(0x4B000000u | u) - (8388608.0f + off);
+}
 
 // ------------------------------------------------------------ dequant
 // One thread per 32-value block.
@@ -61,14 +64,14 @@ __global__ void dequant_q_kernel(const uint8_t *__restrict__ data, uint64_t n_bl
             for (int i = 0; i < 8; ++i) {
                 const uint32_t two = blk[1 + i];  // bytes 2i, 2i+1 of the 16 nibble bytes
 #pragma unroll
-                for (int k = 0; k < 4; ++k) v[4 * i + k] = (magic_u((two >> (4 * k)) & 15u) - 8.0f) * scale;
+                for (int k = 0; k < 4; ++k) v[4 * i + k] = magic_u((two >> (4 * k)) & 15u, 8.0f) * scale;
             }
         } else {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
                 const uint32_t two = blk[1 + i];
 #pragma unroll
-                for (int k = 0; k < 2; ++k) v[2 * i + k] = (magic_u(((two >> (8 * k)) & 255u) ^ 128u) - 128.0f) * scale;
+                for (int k = 0; k < 2; ++k) v[2 * i + k] = magic_u(((two >> (8 * k)) & 255u) ^ 128u, 128.0f) * scale;
             }
         }
     } else {
@@ -106,8 +109,7 @@ struct Block32 {
             for (int i = 0; i < 8; ++i) {
                 const uint32_t two = __ldg(blk + 1 + i);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) acc[4 * i + k] = fmaf(xs, magic_u((two >> (4 * k)) & 15u) - 8.0f,
-                                                                  acc[4 * i + k]);
+                for (int k = 0; k < 4; ++k) acc[4 * i + k] = fmaf(xs, magic_u((two >> (4 * k)) & 15u, 8.0f), acc[4 * i + k]);
             }
         } else {
 #pragma unroll
@@ -115,7 +117,7 @@ struct Block32 {
                 const uint32_t two = __ldg(blk + 1 + i);
 #pragma unroll
                 for (int k = 0; k < 2; ++k)
-                    acc[2 * i + k] = fmaf(xs, magic_u(((two >> (8 * k)) & 255u) ^ 128u) - 128.0f, acc[2 * i + k]);
+                    acc[2 * i + k] = fmaf(xs, magic_u(((two >> (8 * k)) & 255u) ^ 128u, 128.0f), acc[2 * i + k]);
             }
         }
     }
@@ -191,6 +193,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t *__res
 #pragma unroll
     for (int i = 0; i < 32; ++i) acc[i] = 0.f;
     if (cb < n_cb) {
+#pragma unroll 4
         for (uint64_t r = r0 + rp; r < r1; r += kRowPhases) Block32<QT>::fma(w, r, n_out, cb, n_ok, __ldg(x + r), acc);
     }
 #pragma unroll
@@ -203,6 +206,155 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t *__res
 #pragma unroll 8
         for (int k = 0; k < kRowPhases; ++k) s += (double)part[k][tid];
         dst[(uint64_t)blockIdx.y * n_out + j] = s;
+    }
+}
+
+// ---- staged GEMV: 1024-column tiles, row segments streamed through a
+// cp.async ring in shared memory.  Used when n_out % 256 == 0, W is 16-byte
+// aligned and the data holds the whole tensor (rows are then 16-byte
+// aligned runs of n_out/32 blocks).  The direct kernel above has each
+// thread wait on its own scattered 2-byte loads, one row after another;
+// here 256 threads keep three stages of whole row segments in flight.
+// Thread t owns 32-column block t % 32 of the tile and rows t / 32 (mod 8)
+// of each stage.
+constexpr int kTileBlocks = 32;
+constexpr int kRing = 3;
+
+template <int QT>
+struct StagedCfg {
+    static constexpr uint32_t BB = QT == kGgufQ4_0 ? 18u : QT == kGgufQ8_0 ? 34u : QT == kGgufF16 ? 64u : 128u;
+    static constexpr uint32_t SEG = kTileBlocks * BB;  // bytes of one row of a tile
+    static constexpr uint32_t RS_RAW = 18432u / SEG;
+    static constexpr uint32_t RS = RS_RAW < 8u ? 8u : (RS_RAW / 8u) * 8u;  // rows per stage
+    static constexpr uint32_t STAGE = RS * SEG;
+    static constexpr uint32_t SMEM = kRing * STAGE > 8u * 1024u * 4u ? kRing * STAGE : 8u * 1024u * 4u;
+};
+
+__device__ __forceinline__ void cp16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// acc += x * (the 32 values of one block at shared address blk)
+template <int QT>
+__device__ __forceinline__ void block_fma_smem(const uint8_t *blk, float x, float acc[32]) {
+    if constexpr (QT == kGgufQ4_0 || QT == kGgufQ8_0) {
+        const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
+        const float xs = x * f16_bits_to_f32(h[0]);
+        if constexpr (QT == kGgufQ4_0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const uint32_t two = h[1 + i];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) acc[4 * i + k] = fmaf(xs, magic_u((two >> (4 * k)) & 15u, 8.0f), acc[4 * i + k]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const uint32_t two = h[1 + i];
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+                    acc[2 * i + k] = fmaf(xs, magic_u(((two >> (8 * k)) & 255u) ^ 128u, 128.0f), acc[2 * i + k]);
+            }
+        }
+    } else if constexpr (QT == kGgufF16) {
+        const uint4 *q4 = reinterpret_cast<const uint4 *>(blk);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint4 q = q4[i];
+            const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[k]));
+                acc[8 * i + 2 * k] = fmaf(x, f.x, acc[8 * i + 2 * k]);
+                acc[8 * i + 2 * k + 1] = fmaf(x, f.y, acc[8 * i + 2 * k + 1]);
+            }
+        }
+    } else {
+        const float4 *f4 = reinterpret_cast<const float4 *>(blk);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 q = f4[i];
+            acc[4 * i] = fmaf(x, q.x, acc[4 * i]);
+            acc[4 * i + 1] = fmaf(x, q.y, acc[4 * i + 1]);
+            acc[4 * i + 2] = fmaf(x, q.z, acc[4 * i + 2]);
+            acc[4 * i + 3] = fmaf(x, q.w, acc[4 * i + 3]);
+        }
+    }
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t *__restrict__ w, uint64_t n_out,
+                                                                   uint64_t rows, uint64_t rows_per_range,
+                                                                   const double *__restrict__ x,
+                                                                   double *__restrict__ dst) {
+    using Cf = StagedCfg<QT>;
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int tid = threadIdx.x;
+    const int cbl = tid % kTileBlocks, rp = tid / kTileBlocks;  // 8 row phases
+    const uint64_t n_cb = n_out / 32;
+    const uint64_t row_bytes = n_cb * Cf::BB;
+    const uint64_t cb0 = (uint64_t)blockIdx.x * kTileBlocks;
+    // blocks of this tile: a multiple of 8 (n_out % 256 == 0)
+    const uint32_t tile_blocks = (uint32_t)(n_cb - cb0 < (uint64_t)kTileBlocks ? n_cb - cb0 : (uint64_t)kTileBlocks);
+    const uint32_t seg_chunks = tile_blocks * Cf::BB / 16u;
+    const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_range;
+    const uint64_t r1 = min(r0 + rows_per_range, rows);
+    const uint32_t n_stages = (uint32_t)((r1 - r0 + Cf::RS - 1) / Cf::RS);
+    const uint8_t *tile = w + cb0 * Cf::BB;
+    const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(sm);
+
+    auto stage_rows = [&](uint32_t st) {
+        const uint64_t rb = r0 + (uint64_t)st * Cf::RS;
+        return (uint32_t)(r1 - rb < (uint64_t)Cf::RS ? r1 - rb : (uint64_t)Cf::RS);
+    };
+    auto issue = [&](uint32_t st) {  // rows [r0 + st*RS, ...) into ring slot st % kRing
+        if (st < n_stages) {
+            const uint64_t rb = r0 + (uint64_t)st * Cf::RS;
+            const uint32_t nr = stage_rows(st);
+            const uint32_t slot = smem0 + (st % kRing) * Cf::STAGE;
+            for (uint32_t c = tid; c < nr * seg_chunks; c += kGemvThreads) {
+                const uint32_t rr = c / seg_chunks, cc = c % seg_chunks;
+                cp16(slot + rr * Cf::SEG + cc * 16u, tile + (rb + rr) * row_bytes + cc * 16u);
+            }
+        }
+        cp_commit();  // one group per stage, empty past the end
+    };
+
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll
+    for (int st = 0; st < kRing - 1; ++st) issue(st);
+    for (uint32_t st = 0; st < n_stages; ++st) {
+        issue(st + kRing - 1);
+        cp_wait<kRing - 1>();  // stage st has landed (this thread's copies)
+        __syncthreads();       // ... and every thread's
+        const uint64_t rb = r0 + (uint64_t)st * Cf::RS;
+        const uint32_t nr = stage_rows(st);
+        if ((uint32_t)cbl < tile_blocks) {
+            const uint8_t *slot = sm + (st % kRing) * Cf::STAGE;
+            for (uint32_t rr = rp; rr < nr; rr += kGemvThreads / kTileBlocks)
+                block_fma_smem<QT>(slot + rr * Cf::SEG + cbl * Cf::BB, (float)__ldg(x + rb + rr), acc);
+        }
+        __syncthreads();  // the slot is refilled next iteration
+    }
+    cp_wait<0>();
+    __syncthreads();
+    // the 8 row phases of each column, summed in f64 in phase order
+    float *part = reinterpret_cast<float *>(sm);  // [8][1024]
+#pragma unroll
+    for (int i = 0; i < 32; ++i) part[rp * 1024 + cbl * 32 + i] = acc[i];
+    __syncthreads();
+    for (uint32_t c = tid; c < tile_blocks * 32u; c += kGemvThreads) {
+        double sacc = 0.0;
+#pragma unroll
+        for (int k = 0; k < kGemvThreads / kTileBlocks; ++k) sacc += (double)part[k * 1024 + c];
+        dst[(uint64_t)blockIdx.y * n_out + cb0 * 32 + c] = sacc;
     }
 }
 
@@ -260,10 +412,12 @@ cudaError_t read_tensor_f32(const void *data, uint64_t data_len, int gguf_type, 
     }
 }
 
-GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms) {
+GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms, bool staged) {
     GemvPlan pl;
     pl.rows = x_len < n_in ? x_len : n_in;
-    pl.col_tiles = (n_out + kCols - 1) / kCols;
+    pl.staged = staged;
+    const uint64_t cols = staged ? (uint64_t)kTileBlocks * 32 : (uint64_t)kCols;
+    pl.col_tiles = (n_out + cols - 1) / cols;
     // enough CTAs for ~2 per SM, at least 128 rows a range, at most 32 ranges
     uint64_t ranges = (2ull * num_sms + pl.col_tiles - 1) / pl.col_tiles;
     const uint64_t by_rows = (pl.rows + 127) / 128;
@@ -277,9 +431,39 @@ GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms) {
 
 size_t gemv_workspace_bytes(uint64_t n_out) { return (size_t)32 * n_out * sizeof(double); }
 
+bool gemv_staged_ok(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in, uint64_t n_out) {
+    const bool quant = gguf_type == kGgufQ4_0 || gguf_type == kGgufQ8_0;
+    const uint64_t n = n_in * n_out;
+    const uint64_t have = quant ? gguf_blocks_ok(gguf_type, data_len, n) * 32 : gguf_values_read(gguf_type, data_len, n);
+    return n_out % 256 == 0 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && have >= n;
+}
+
+namespace {
+
+template <int QT>
+cudaError_t launch_staged(const uint8_t *w, uint64_t n_out, const GemvPlan &pl, const double *x, double *dst,
+                          cudaStream_t st) {
+    using Cf = StagedCfg<QT>;
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(gemv_staged_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    gemv_staged_kernel<QT><<<dim3((unsigned)pl.col_tiles, pl.ranges), kGemvThreads, Cf::SMEM, st>>>(
+        w, n_out, pl.rows, pl.rows_per_range, x, dst);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in, uint64_t n_out, const double *x,
                  uint64_t x_len, double *y, double *partial, int num_sms, cudaStream_t st) {
-    const GemvPlan pl = gemv_plan(n_in, n_out, x_len, num_sms);
+    const bool staged = gemv_staged_ok(w, data_len, gguf_type, n_in, n_out);
+    const GemvPlan pl = gemv_plan(n_in, n_out, x_len, num_sms, staged);
     if (pl.rows == 0) return cudaMemsetAsync(y, 0, n_out * sizeof(double), st);
     uint64_t n_ok = 0;
     if (gguf_type == kGgufQ4_0 || gguf_type == kGgufQ8_0) {
@@ -291,6 +475,19 @@ cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in,
     double *dst = pl.ranges == 1 ? y : partial;
     const dim3 grid((unsigned)pl.col_tiles, pl.ranges);
     const uint8_t *wb = static_cast<const uint8_t *>(w);
+    if (staged) {
+        cudaError_t se = cudaSuccess;
+        switch (gguf_type) {
+            case kGgufF32: se = launch_staged<kGgufF32>(wb, n_out, pl, x, dst, st); break;
+            case kGgufF16: se = launch_staged<kGgufF16>(wb, n_out, pl, x, dst, st); break;
+            case kGgufQ4_0: se = launch_staged<kGgufQ4_0>(wb, n_out, pl, x, dst, st); break;
+            case kGgufQ8_0: se = launch_staged<kGgufQ8_0>(wb, n_out, pl, x, dst, st); break;
+            default: return cudaErrorInvalidValue;
+        }
+        if (se != cudaSuccess || pl.ranges == 1) return se;
+        gemv_reduce_kernel<<<(unsigned)((n_out + 255) / 256), 256, 0, st>>>(partial, pl.ranges, n_out, y);
+        return cudaGetLastError();
+    }
     switch (gguf_type) {
         case kGgufF32: gemv_kernel<kGgufF32><<<grid, kGemvThreads, 0, st>>>(wb, n_ok, n_out, pl.rows, pl.rows_per_range, x, dst); break;
         case kGgufF16: gemv_kernel<kGgufF16><<<grid, kGemvThreads, 0, st>>>(wb, n_ok, n_out, pl.rows, pl.rows_per_range, x, dst); break;

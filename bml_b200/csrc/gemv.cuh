@@ -19,11 +19,15 @@ cudaError_t read_tensor_f32(const void *data, uint64_t data_len, int gguf_type, 
 
 struct GemvPlan {
     uint64_t rows;            // min(x_len, n_in)
-    uint64_t col_tiles;       // 256-column tiles
+    bool staged;              // 1024-column tiles through a shared-memory ring
+    uint64_t col_tiles;       // 256- (or 1024-, staged) column tiles
     uint64_t rows_per_range;
     uint32_t ranges;          // row ranges summed by gemv_reduce_kernel
 };
-GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms);
+GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms, bool staged);
+// The staged kernel applies: n_out % 256 == 0, W 16-byte aligned, and the
+// data holds the whole n_in x n_out tensor.
+bool gemv_staged_ok(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in, uint64_t n_out);
 // Scratch for the row-range partials: at most 32 ranges of n_out doubles.
 size_t gemv_workspace_bytes(uint64_t n_out);
 

@@ -2,8 +2,9 @@
 gguf_compiler.rs: read_tensor_f32 (:351-470) bit for bit on random bytes
 (every f16 scale pattern, truncated data, element counts that are not a
 multiple of 32), and matmul_f64 (:1239-1255) read straight from the stored
-tensor, within 1e-6 of sum_i |x_i W_ij| (terms and partial sums are f32 on
-the device, f64 in the reference) plus 1e-12."""
+tensor -- by the staged kernel (n_out % 256 == 0) and the direct one --
+within 1e-6 of sum_i |x_i W_ij| (terms and partial sums are f32 on the
+device, f64 in the reference) plus 1e-12."""
 import numpy as np
 import pytest
 import torch
@@ -75,6 +76,9 @@ def weight_bytes(rng, gguf_type, n_in, n_out):
     (oracle.GGUF_F16, 512, 1000, 512),    # n_out not a multiple of 32
     (oracle.GGUF_F32, 777, 333, 777),
     (oracle.GGUF_F32, 1, 1, 1),
+    (oracle.GGUF_F16, 520, 768, 520),     # staged kernel, f16
+    (oracle.GGUF_F32, 300, 512, 300),     # staged kernel, f32
+    (oracle.GGUF_Q4_0, 37, 2304, 37),     # staged, a partial last tile, one row range
 ])
 def test_matmul_f64_matches_oracle(cuda, gguf_type, n_in, n_out, x_len):
     import bml_b200
