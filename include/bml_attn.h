@@ -195,8 +195,11 @@ bml_status bml_kv_append_rope_batched(const bml_seq_desc *seqs_host,
                                       const float *k_new_dev,
                                       const float *v_new_dev, void *stream);
 
-/* Scratch bytes bml_attn_decode_batched / _partial need for n_seqs
- * sequences on `device`. */
+/* Scratch bytes recommended for bml_attn_decode_batched / _partial with
+ * n_seqs sequences on `device`: room for the partial results of about 8
+ * work chunks per SM.  A smaller workspace down to 2 * n_seqs + (SM count)
+ * slots still works (the kernels then cut the work into fewer, larger
+ * chunks); below that the call returns BML_E_INVALID. */
 bml_status bml_attn_decode_workspace_size(uint32_t n_seqs, uint32_t n_heads,
                                           uint32_t head_dim, int32_t device,
                                           size_t *bytes);
@@ -227,9 +230,11 @@ bml_status bml_attn_decode_batched(const bml_seq_desc *seqs_host,
  * device-wide synchronisation would stall other streams.  It takes no
  * workspace; its scratch is a fixed 4 MiB array in device global memory
  * that every GPU loading this library holds until the process exits, and it
- * allocates nothing itself.  A call that would need more scratch than that
- * (bml_attn_decode_workspace_size for the same arguments above 4 MiB, e.g.
- * 256 sequences of 64 heads at head_dim 128) returns BML_E_INVALID.  The
+ * allocates nothing itself.  A call whose smallest usable scratch -- split
+ * slots for 2 * n_seqs + (SM count) partial results of n_heads rows of
+ * head_dim + 2 floats, plus 8.5 KiB of tickets -- is above 4 MiB (e.g. 256
+ * sequences of 64 heads at head_dim 128) returns BML_E_INVALID; below that
+ * the kernels size their work to the slots the array holds.  The
  * first call on a device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture.
  * All calls share the one array, which keeps the last call's contents: each
