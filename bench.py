@@ -26,6 +26,11 @@ is already resident in HBM.  Workloads (--workload):
                            step is one layer's 7 projections, cycling over 4
                            layers of distinct weights (490 MB > L2).  Metric:
                            HBM GB/s of stored weight bytes + x/y ("weak").
+  gguf_load                a GGUF file of 8 Llama-3-8B layers' projections
+                           (Q4_0, 0.98 GB) uploaded to the device by
+                           bml_gguf_upload (memory-mapped file, pinned
+                           staging, 4 host threads).  Metric: GB/s of tensor
+                           bytes into device memory (page cache warm).
   serving                  continuous batching (DecodeBatcher): 32 requests
                            of Llama-3-8B shape (32 layers, 32/8 heads,
                            d=128, bf16 KV), prompts U[1024,4096]; a step is
@@ -440,6 +445,8 @@ def run_b200(args):
         return run_serving(args, dist, peaks, res)
     elif wl == "gemv":
         return run_gemv(args, dist, peaks, res)
+    elif wl == "gguf_load":
+        return run_gguf_load(args, dist, peaks, res)
     else:
         raise SystemExit(f"unknown workload {wl}")
 
@@ -729,6 +736,92 @@ def run_gemv(args, dist, peaks, res):
     emit(res, dist)
 
 
+def cpu_gguf_sample(path, budget_s: float):
+    """What the reference does with a loaded tensor: read_tensor_f32 into
+    its f32 pool (the oracle's dequantize_q4_0, one thread)."""
+    import oracle
+    from bml_b200 import gguf
+    with gguf.GgufFile(path) as f:
+        info = f.find_tensor("blk.0.attn_q.weight")
+        view = f.tensor_data(info)[:info.nbytes].tobytes()
+    n = info.dims[0] * info.dims[1]
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.read_tensor_f32(view, oracle.GGUF_Q4_0, n)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return len(view) / dt / 1e9, 1, f"attn_q 4096x4096 Q4_0 to f32 (1 thread), {reps} passes, {dt * 1e3:.1f} ms/pass"
+
+
+def run_gguf_load(args, dist, peaks, res):
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    from bml_b200 import gguf
+    dev = dist.device
+    n_layers = 8
+    rng = np.random.default_rng(9 + dist.rank)
+    block = rng.integers(0, 256, 32 << 20, dtype=np.uint8)  # 32 MiB of random bytes, reused
+    tensors = []
+    for layer in range(n_layers):
+        for nm, a, b in GEMV_LAYER:
+            nbytes = a * b // 32 * 18
+            reps = -(-nbytes // block.size)
+            tensors.append((f"blk.{layer}.{nm}.weight", [a, b], 2, np.tile(block, reps)[:nbytes]))
+    tmpdir = tempfile.mkdtemp(prefix="bml_gguf_")
+    path = os.path.join(tmpdir, f"model_{dist.rank}.gguf")
+    gguf.write_gguf(path, [("general.architecture", 8, "llama"), ("llama.block_count", 4, n_layers)], tensors)
+    del tensors
+    f = gguf.GgufFile(path)
+    infos = f.tensor_infos
+    bufs = [torch.empty(i.nbytes, dtype=torch.uint8, device=dev) for i in infos]
+    import ctypes as C
+    from bml_b200 import _lib as L
+    idx = (C.c_uint64 * len(infos))(*[i.index for i in infos])
+    dst = (C.c_void_p * len(infos))(*[b.data_ptr() for b in bufs])
+    total_bytes = sum(i.nbytes for i in infos)
+    torch.cuda.synchronize()
+
+    def step():
+        L.call("bml_gguf_upload", f._h, idx, len(infos), dst, 4)
+
+    ms, clocks = timed_loop(step, args.steps, args.warmup, dist, dist.local)
+    gbs = dist.sum(total_bytes) * args.steps / (ms * 1e-3) / 1e9
+    # the copy engine's own rate: one 256 MiB pinned buffer to the device
+    pin = torch.empty(256 << 20, dtype=torch.uint8).pin_memory()
+    dbuf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    dbuf.copy_(pin, non_blocking=True)
+    torch.cuda.synchronize()
+    h2d_ms = kernel_ms(lambda: dbuf.copy_(pin, non_blocking=True), reps=10)
+    h2d = pin.numel() / (h2d_ms * 1e-3) / 1e9
+    ach = total_bytes / (ms / args.steps * 1e-3) / 1e9
+    ok = all(torch.equal(bufs[k][:64].cpu(), torch.from_numpy(f.tensor_data(infos[k])[:64].copy())) for k in (0, -1))
+    res.update({"metric": "GGUF upload GB/s (host file -> device)", "value": round(gbs, 2), "unit": "GB/s",
+                "ms_per_step": round(ms / args.steps, 3), "scaling": "weak", "dtype": "u8 (Q4_0 bytes)",
+                "config": {"workload": "gguf_load", "tensors": len(infos), "file_bytes": f.file_size,
+                           "tensor_bytes": total_bytes, "layers": n_layers, "threads": 4, "page_cache": "warm",
+                           "bytes_verified": bool(ok)},
+                "roofline": {"bound": "h2d", "achieved": round(ach, 2), "peak": round(h2d, 2), "unit": "GB/s",
+                             "frac": round(ach / h2d, 4), "traffic": None,
+                             "peak_source": "pinned 256 MiB cudaMemcpyAsync to the device, measured in this run"},
+                "clocks": clocks,
+                "e2e": {"value": round(gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": total_bytes,
+                        "d2h_bytes_per_step": 0},
+                "gpu_launches": 0})
+    if dist.world == 1 and not args.no_cpu:
+        v, thr, desc = cpu_gguf_sample(path, args.cpu_budget)
+        res["cpu_baseline"] = {"value": round(v, 4), "unit": "GB/s", "cores": thr, "kind": "port", "sample": desc}
+    f.close()
+    os.remove(path)
+    os.rmdir(tmpdir)
+    emit(res, dist)
+
+
 def run_serving(args, dist, peaks, res):
     """DecodeBatcher over 32 Llama-3-shaped requests; one step = one token of
     every request through all layers, with a leave + join every 8 steps."""
@@ -888,7 +981,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--workload", default="llama3_decode",
-                    choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill", "serving", "gemv"])
+                    choices=["llama3_decode", "batched_tinyllama", "longctx", "llama3_prefill", "serving", "gemv",
+                             "gguf_load"])
     ap.add_argument("--prefill-steps", type=int, default=200)
     ap.add_argument("--prefill-n", type=int, default=4, help="prefill sequences (llama3_prefill)")
     ap.add_argument("--prefill-s", type=int, default=8192, help="prefill tokens per sequence")

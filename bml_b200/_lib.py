@@ -45,7 +45,24 @@ class bml_seq_desc(C.Structure):
                 ("reserved", C.c_uint32)]
 
 
-# name -> (restype, argtypes); mirrors include/bml_attn.h one to one.
+class bml_gguf_header(C.Structure):
+    _fields_ = [("magic", C.c_uint32), ("version", C.c_uint32), ("tensor_count", C.c_uint64),
+                ("metadata_kv_count", C.c_uint64), ("data_offset", C.c_uint64), ("file_size", C.c_uint64)]
+
+
+class bml_gguf_tensor(C.Structure):
+    _fields_ = [("name", C.c_void_p), ("name_len", C.c_uint64), ("n_dims", C.c_uint32), ("type", C.c_uint32),
+                ("dims", C.POINTER(C.c_uint64)), ("offset", C.c_uint64), ("present", C.c_int32),
+                ("data_offset", C.c_uint64), ("view_len", C.c_uint64), ("nbytes", C.c_uint64)]
+
+
+class bml_gguf_value(C.Structure):
+    _fields_ = [("type", C.c_uint32), ("elem_type", C.c_uint32), ("len", C.c_uint64), ("u", C.c_uint64),
+                ("i", C.c_int64), ("f", C.c_double), ("str", C.c_void_p)]
+
+
+# name -> (restype, argtypes); mirrors include/bml_attn.h, bml_weights.h and
+# bml_gguf.h one to one.
 _vp, _u32, _i32, _st, _sz = C.c_void_p, C.c_uint32, C.c_int32, C.c_int32, C.c_size_t
 GGUF_F32, GGUF_F16, GGUF_Q4_0, GGUF_Q8_0 = 0, 1, 2, 8  # include/bml_weights.h
 SIGNATURES = {
@@ -86,6 +103,17 @@ SIGNATURES = {
     "bml_read_tensor_f32": (_st, [_vp, C.c_uint64, _i32, C.c_uint64, _vp, C.POINTER(C.c_uint64), _vp]),
     "bml_matmul_workspace_size": (_st, [C.c_uint64, C.POINTER(_sz)]),
     "bml_matmul_f64": (_st, [_vp, C.c_uint64, _i32, C.c_uint64, C.c_uint64, _vp, C.c_uint64, _vp, _vp, _sz, _vp]),
+    # include/bml_gguf.h
+    "bml_gguf_open": (_st, [C.c_char_p, C.POINTER(_vp)]),
+    "bml_gguf_close": (_st, [_vp]),
+    "bml_gguf_get_header": (_st, [_vp, C.POINTER(bml_gguf_header)]),
+    "bml_gguf_tensor_info": (_st, [_vp, C.c_uint64, C.POINTER(bml_gguf_tensor)]),
+    "bml_gguf_find_tensor": (_st, [_vp, C.c_char_p, C.POINTER(C.c_uint64)]),
+    "bml_gguf_tensor_view": (_st, [_vp, C.c_uint64, C.POINTER(_vp), C.POINTER(C.c_uint64)]),
+    "bml_gguf_meta_key": (_st, [_vp, C.c_uint64, C.POINTER(_vp), C.POINTER(C.c_uint64)]),
+    "bml_gguf_meta_find": (_st, [_vp, C.c_char_p, C.POINTER(C.c_uint64)]),
+    "bml_gguf_meta_value": (_st, [_vp, C.c_uint64, C.POINTER(C.c_uint64), _u32, C.POINTER(bml_gguf_value)]),
+    "bml_gguf_upload": (_st, [_vp, C.POINTER(C.c_uint64), _u32, C.POINTER(_vp), _u32]),
     "bml_diag_exp2": (_st, [_vp, _u32, C.c_int, _vp, _vp]),
     "bml_attn_workspace_check": (_st, [_vp, _sz, _vp]),
 }

@@ -60,6 +60,25 @@ bml_status cuda_fail(cudaError_t e, const char *what) {
 
 bool valid_dtype(int t) { return t == BML_F32 || t == BML_F16 || t == BML_BF16; }
 
+}  // namespace
+
+// The status helpers for the other host files of the library (gguf.cu).
+namespace bml {
+bml_status api_fail(bml_status code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+bml_status api_ok() { return ok(); }
+bml_status api_cuda_fail(cudaError_t e, const char *where) { return cuda_fail(e, where); }
+}  // namespace bml
+
+namespace {
+
 int num_sms(int device) {
     static std::mutex mu;
     static int cache[64] = {0};
