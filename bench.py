@@ -29,7 +29,7 @@ is already resident in HBM.  Workloads (--workload):
   gguf_load                a GGUF file of 8 Llama-3-8B layers' projections
                            (Q4_0, 0.98 GB) uploaded to the device by
                            bml_gguf_upload (memory-mapped file, pinned
-                           staging, 4 host threads).  Metric: GB/s of tensor
+                           staging, 8 host threads).  Metric: GB/s of tensor
                            bytes into device memory (page cache warm).
   serving                  continuous batching (DecodeBatcher): 32 requests
                            of Llama-3-8B shape (32 layers, 32/8 heads,
@@ -788,7 +788,7 @@ def run_gguf_load(args, dist, peaks, res):
     torch.cuda.synchronize()
 
     def step():
-        L.call("bml_gguf_upload", f._h, idx, len(infos), dst, 4)
+        L.call("bml_gguf_upload", f._h, idx, len(infos), dst, args.gguf_threads)
 
     ms, clocks = timed_loop(step, args.steps, args.warmup, dist, dist.local)
     gbs = dist.sum(total_bytes) * args.steps / (ms * 1e-3) / 1e9
@@ -804,7 +804,8 @@ def run_gguf_load(args, dist, peaks, res):
     res.update({"metric": "GGUF upload GB/s (host file -> device)", "value": round(gbs, 2), "unit": "GB/s",
                 "ms_per_step": round(ms / args.steps, 3), "scaling": "weak", "dtype": "u8 (Q4_0 bytes)",
                 "config": {"workload": "gguf_load", "tensors": len(infos), "file_bytes": f.file_size,
-                           "tensor_bytes": total_bytes, "layers": n_layers, "threads": 4, "page_cache": "warm",
+                           "tensor_bytes": total_bytes, "layers": n_layers, "threads": args.gguf_threads,
+                           "page_cache": "warm",
                            "bytes_verified": bool(ok)},
                 "roofline": {"bound": "h2d", "achieved": round(ach, 2), "peak": round(h2d, 2), "unit": "GB/s",
                              "frac": round(ach / h2d, 4), "traffic": None,
@@ -987,6 +988,7 @@ def main():
     ap.add_argument("--prefill-n", type=int, default=4, help="prefill sequences (llama3_prefill)")
     ap.add_argument("--prefill-s", type=int, default=8192, help="prefill tokens per sequence")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--gguf-threads", type=int, default=8, help="host threads of bml_gguf_upload (gguf_load)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     args = ap.parse_args()

@@ -37,6 +37,7 @@ constexpr int kGemvThreads = 256;
 constexpr int kColBlocks = 8;                  // 32-column blocks per CTA
 constexpr int kCols = kColBlocks * 32;         // columns per CTA
 constexpr int kRowPhases = kGemvThreads / kColBlocks;  // 32
+constexpr uint64_t kMaxRanges = 64;                   // row ranges of one GEMV
 
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
@@ -338,8 +339,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
         const uint32_t nr = stage_rows(st);
         if ((uint32_t)cbl < tile_blocks) {
             const uint8_t *slot = sm + (st % kRing) * Cf::STAGE;
-            for (uint32_t rr = rp; rr < nr; rr += kGemvThreads / kTileBlocks)
-                block_fma_smem<QT>(slot + rr * Cf::SEG + cbl * Cf::BB, (float)__ldg(x + rb + rr), acc);
+            constexpr uint32_t kStep = kGemvThreads / kTileBlocks;
+            if (nr == Cf::RS) {  // full stage: a fixed trip count, unrolled for independent loads
+#pragma unroll
+                for (uint32_t k = 0; k < Cf::RS / kStep; ++k) {
+                    const uint32_t rr = rp + k * kStep;
+                    block_fma_smem<QT>(slot + rr * Cf::SEG + cbl * Cf::BB, (float)__ldg(x + rb + rr), acc);
+                }
+            } else {
+                for (uint32_t rr = rp; rr < nr; rr += kStep)
+                    block_fma_smem<QT>(slot + rr * Cf::SEG + cbl * Cf::BB, (float)__ldg(x + rb + rr), acc);
+            }
         }
         __syncthreads();  // the slot is refilled next iteration
     }
@@ -418,18 +428,20 @@ GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms, b
     pl.staged = staged;
     const uint64_t cols = staged ? (uint64_t)kTileBlocks * 32 : (uint64_t)kCols;
     pl.col_tiles = (n_out + cols - 1) / cols;
-    // enough CTAs for ~2 per SM, at least 128 rows a range, at most 32 ranges
-    uint64_t ranges = (2ull * num_sms + pl.col_tiles - 1) / pl.col_tiles;
-    const uint64_t by_rows = (pl.rows + 127) / 128;
+    // enough CTAs for ~4 per SM (the staged kernel fits 3 per SM; the rest
+    // of the grid fills the gaps), at least 64 rows a range, at most
+    // kMaxRanges ranges
+    uint64_t ranges = (4ull * num_sms + pl.col_tiles - 1) / pl.col_tiles;
+    const uint64_t by_rows = (pl.rows + 63) / 64;
     if (ranges > by_rows) ranges = by_rows;
-    if (ranges > 32) ranges = 32;
+    if (ranges > kMaxRanges) ranges = kMaxRanges;
     if (ranges < 1) ranges = 1;
     pl.rows_per_range = (pl.rows + ranges - 1) / ranges;
     pl.ranges = pl.rows_per_range ? (uint32_t)((pl.rows + pl.rows_per_range - 1) / pl.rows_per_range) : 1;
     return pl;
 }
 
-size_t gemv_workspace_bytes(uint64_t n_out) { return (size_t)32 * n_out * sizeof(double); }
+size_t gemv_workspace_bytes(uint64_t n_out) { return (size_t)kMaxRanges * n_out * sizeof(double); }
 
 bool gemv_staged_ok(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in, uint64_t n_out) {
     const bool quant = gguf_type == kGgufQ4_0 || gguf_type == kGgufQ8_0;

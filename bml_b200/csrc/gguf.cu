@@ -11,11 +11,11 @@
 // "offset fuera de rango" errors).
 //
 // Upload.  A model's tensors are gigabytes read once: each of `threads`
-// host threads owns one pinned staging buffer and one stream, copies a
-// 32 MiB piece of the mapping into its buffer (the CPU read from the page
-// cache) and queues its DMA to the device, so page-in and memcpy of one
-// piece overlap the transfers of the others.  One cudaMemcpyAsync per
-// piece.
+// host threads (8 by default) owns one pinned staging buffer and one
+// stream, copies a 32 MiB piece of the mapping into its buffer (the CPU
+// read from the page cache, ~4-8 GB/s per thread) and queues its DMA to
+// the device, so the pieces' page-in and memcpy run side by side and
+// overlap the transfers of the others.  One cudaMemcpyAsync per piece.
 #include <cuda_runtime.h>
 #include <fcntl.h>
 #include <stdio.h>
@@ -436,7 +436,7 @@ BML_API bml_status bml_gguf_upload(bml_gguf *g, const uint64_t *indices, uint32_
     if (pieces.empty()) return bml::api_ok();
     int dev = 0;
     CUDA_TRY_API(cudaGetDevice(&dev), fn);
-    const uint32_t nt = threads ? std::min<uint32_t>(threads, 16) : 4;
+    const uint32_t nt = threads ? std::min<uint32_t>(threads, 16) : 8;
     if (g->staging_device != dev || g->staging.size() < nt) {  // (re)create the staging set on this device
         if (g->staging_device >= 0) {
             cudaSetDevice(g->staging_device);

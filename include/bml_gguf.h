@@ -121,8 +121,9 @@ bml_status bml_gguf_meta_value(const bml_gguf *g, uint64_t index, const uint64_t
 /* Copies tensors into device memory: tensor indices[k]'s nbytes bytes to
  * dev_dst[k] (device pointers the caller allocated, on the current device).
  * The bytes go through pinned host staging buffers the handle allocates on
- * first use (4 x 32 MiB, freed by bml_gguf_close), read by `threads` host
- * threads (0 = 4) on their own streams.  Returns once every copy is done.
+ * first use (one of 32 MiB per thread, freed by bml_gguf_close), filled by
+ * `threads` host threads (0 = 8, at most 16) that each queue their copies
+ * on their own stream.  Returns once every copy is done.
  * A tensor whose nbytes is 0 (unknown layout) or that runs past the end of
  * the file is refused before anything is copied. */
 bml_status bml_gguf_upload(bml_gguf *g, const uint64_t *indices, uint32_t n, void *const *dev_dst,
