@@ -302,7 +302,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
     const uint64_t cb0 = (uint64_t)blockIdx.x * kTileBlocks;
     // blocks of this tile: a multiple of 8 (n_out % 256 == 0)
     const uint32_t tile_blocks = (uint32_t)(n_cb - cb0 < (uint64_t)kTileBlocks ? n_cb - cb0 : (uint64_t)kTileBlocks);
-    const uint32_t seg_chunks = tile_blocks * Cf::BB / 16u;
+    const uint32_t seg_chunks = tile_blocks * Cf::BB / 16u;  // <= 256
+    const float inv_seg = 1.0f / (float)seg_chunks;
     const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_range;
     const uint64_t r1 = min(r0 + rows_per_range, rows);
     const uint32_t n_stages = (uint32_t)((r1 - r0 + Cf::RS - 1) / Cf::RS);
@@ -319,7 +320,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
             const uint32_t nr = stage_rows(st);
             const uint32_t slot = smem0 + (st % kRing) * Cf::STAGE;
             for (uint32_t c = tid; c < nr * seg_chunks; c += kGemvThreads) {
-                const uint32_t rr = c / seg_chunks, cc = c % seg_chunks;
+                // c / seg_chunks without an integer division: c < 2^13 and
+                // (c + 1/2) / seg_chunks stays at least 1/512 from an integer
+                const uint32_t rr = (uint32_t)(((float)c + 0.5f) * inv_seg);
+                const uint32_t cc = c - rr * seg_chunks;
                 cp16(slot + rr * Cf::SEG + cc * 16u, tile + (rb + rr) * row_bytes + cc * 16u);
             }
         }
@@ -465,8 +469,8 @@ cudaError_t launch_staged(const uint8_t *w, uint64_t n_out, const GemvPlan &pl, 
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    gemv_staged_kernel<QT><<<dim3((unsigned)pl.col_tiles, pl.ranges), kGemvThreads, Cf::SMEM, st>>>(
-        w, n_out, pl.rows, pl.rows_per_range, x, dst);
+    const dim3 grid((unsigned)pl.col_tiles, pl.ranges);
+    gemv_staged_kernel<QT><<<grid, kGemvThreads, Cf::SMEM, st>>>(w, n_out, pl.rows, pl.rows_per_range, x, dst);
     return cudaGetLastError();
 }
 
