@@ -155,5 +155,11 @@ def check(status: int, fn: str) -> None:
     raise BmlError(status, fn, msg)
 
 
+_fns: dict = {}
+
+
 def call(fn: str, *args) -> None:
-    check(getattr(lib(), fn)(*args), fn)
+    f = _fns.get(fn)
+    if f is None:
+        f = _fns[fn] = getattr(lib(), fn)
+    check(f(*args), fn)

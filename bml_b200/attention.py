@@ -70,13 +70,17 @@ class Workspace:
         self.device = torch.device("cuda", torch.cuda.current_device() if device is None else
                                    torch.device(device).index or 0)
         self.buf = torch.zeros(0, dtype=torch.uint8, device=self.device)
+        self._sized = None  # the last (n_seqs, n_heads, head_dim) ensured
 
     def ensure(self, n_seqs: int, n_heads: int, head_dim: int) -> "Workspace":
+        if self._sized == (n_seqs, n_heads, head_dim):
+            return self
         size = C.c_size_t()
         L.call("bml_attn_decode_workspace_size", n_seqs, n_heads, head_dim, self.device.index,
                C.byref(size))
         if self.buf.numel() < size.value:
             self.buf = torch.zeros(size.value, dtype=torch.uint8, device=self.device)
+        self._sized = (n_seqs, n_heads, head_dim)
         return self
 
     @property
