@@ -87,6 +87,7 @@ SIGNATURES = {
     "bml_kv_append_rope_batched": (_st, [C.POINTER(bml_seq_desc), _u32, _u32, _u32, _u32, C.c_int, _vp, _vp,
                                          _vp, _vp]),
     "bml_attn_decode": (_st, [_vp, _u32, _u32, _u32, C.c_float, _vp, _vp, _vp]),
+    "bml_attn_decode_wrap": (_st, [_vp, _u32, _u32, _u32, C.c_float, _vp, _vp, _vp]),
     "bml_attn_decode_workspace_size": (_st, [_u32, _u32, _u32, _i32, C.POINTER(_sz)]),
     "bml_attn_decode_batched": (_st, [C.POINTER(bml_seq_desc), _u32, _u32, _u32, _u32, C.c_int,
                                       C.c_float, _vp, _vp, _vp, _sz, _vp]),

@@ -128,6 +128,8 @@ struct bml_kv {
     float *staging = nullptr;  // device scratch: head_dim floats + 1
     void *ws = nullptr;        // decode workspace for bml_attn_decode
     size_t ws_bytes = 0;
+    float *wrap = nullptr;     // bml_attn_decode_wrap: two q copies + two partials
+    size_t wrap_floats = 0;
     size_t layer_elems() const { return (size_t)desc.max_seq_len * desc.n_kv_heads * desc.head_dim; }
     size_t esize() const { return bml::dtype_size(desc.dtype); }
 };
@@ -180,6 +182,7 @@ BML_API bml_status bml_kv_destroy(bml_kv *kv) {
     for (void *p : kv->v) if (p) cudaFree(p);
     if (kv->staging) cudaFree(kv->staging);
     if (kv->ws) cudaFree(kv->ws);
+    if (kv->wrap) cudaFree(kv->wrap);
     delete kv;
     return ok();
 }
@@ -603,6 +606,67 @@ BML_API bml_status bml_attn_decode(bml_kv *kv, uint32_t layer, uint32_t pos, uin
     return decode_impl(&d, 1, n_heads, kv->desc.n_kv_heads, kv->desc.head_dim, kv->desc.dtype, scale, q_dev,
                        out_dev, nullptr, nullptr, nullptr, kv->ws, kv->ws_bytes, stream, bml::kModeFinal,
                        "bml_attn_decode");
+}
+
+BML_API bml_status bml_attn_decode_wrap(bml_kv *kv, uint32_t layer, uint32_t pos, uint32_t n_heads, float scale,
+                                        const float *q_dev, float *out_dev, void *stream) {
+    const char *fn = "bml_attn_decode_wrap";
+    if (!kv) return fail(BML_E_INVALID, "%s: null handle", fn);
+    const uint32_t M = kv->desc.max_seq_len;
+    if (pos < M) return bml_attn_decode(kv, layer, pos, n_heads, scale, q_dev, out_dev, stream);
+    if (layer >= kv->desc.n_layers) return fail(BML_E_INVALID, "%s: layer %u", fn, layer);
+    bml_status st = check_decode_shape(n_heads, kv->desc.n_kv_heads, kv->desc.head_dim, kv->desc.dtype, fn);
+    if (st != BML_OK) return st;
+    if (!q_dev || !out_dev || !aligned16(q_dev)) return fail(BML_E_INVALID, "%s: q and out must be device pointers", fn);
+    DeviceGuard g(kv->desc.device);
+    const uint32_t d = kv->desc.head_dim;
+    // The loop of gguf_compiler.rs:1026 visits positions 0..pos through
+    // slot p % M (kv_cache.rs:83): slot s is visited n/M times, plus once
+    // more for s < n % M (n = pos + 1).  Identical scores give identical
+    // softmax terms, so the result is attention over the M slots with each
+    // slot's weight multiplied by its visit count: two partials (slots
+    // below and from n % M) merged with counts c+1 and c.
+    const uint64_t n = (uint64_t)pos + 1;
+    const uint32_t r = (uint32_t)(n % M);
+    const float c = (float)(n / M);
+    const size_t need_ws = bml::decode_workspace_bytes(2, n_heads, d, num_sms(kv->desc.device));
+    if (kv->ws_bytes < need_ws) {
+        if (kv->ws) cudaFree(kv->ws);
+        kv->ws = nullptr;
+        kv->ws_bytes = 0;
+        CUDA_TRY(cudaMalloc(&kv->ws, need_ws), fn);
+        CUDA_TRY(cudaMemset(kv->ws, 0, need_ws), fn);
+        kv->ws_bytes = need_ws;
+    }
+    const size_t hd = (size_t)n_heads * d;
+    const size_t need_f = 2 * hd + 2 * (2 * n_heads + hd);  // q copies; m, l, o of two parts
+    if (kv->wrap_floats < need_f) {
+        if (kv->wrap) cudaFree(kv->wrap);
+        kv->wrap = nullptr;
+        kv->wrap_floats = 0;
+        CUDA_TRY(cudaMalloc(&kv->wrap, need_f * sizeof(float)), fn);
+        kv->wrap_floats = need_f;
+    }
+    float *qq = kv->wrap, *pm = qq + 2 * hd, *pl = pm + 2 * n_heads, *po = pl + 2 * n_heads;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t row = (size_t)kv->desc.n_kv_heads * d * kv->esize();
+    bml_seq_desc parts[2];
+    uint32_t np = 0;
+    float counts[2];
+    if (r > 0) {
+        parts[np] = {kv->k[layer], kv->v[layer], r, 0};
+        counts[np++] = c + 1.f;
+    }
+    parts[np] = {static_cast<const char *>(kv->k[layer]) + r * row, static_cast<const char *>(kv->v[layer]) + r * row,
+                 M - r, 0};
+    counts[np++] = c;
+    for (uint32_t k = 0; k < np; ++k)
+        CUDA_TRY(cudaMemcpyAsync(qq + k * hd, q_dev, hd * sizeof(float), cudaMemcpyDeviceToDevice, s), fn);
+    st = decode_impl(parts, np, n_heads, kv->desc.n_kv_heads, d, kv->desc.dtype, scale, qq, nullptr, pm, pl, po,
+                     kv->ws, kv->ws_bytes, stream, bml::kModePartial, fn);
+    if (st != BML_OK) return st;
+    CUDA_TRY(bml::launch_merge_counted(pm, pl, po, np, counts, n_heads, d, out_dev, s), fn);
+    return ok();
 }
 
 BML_API bml_status bml_attn_merge_lse(const float *m_dev, const float *l_dev, const float *o_dev, uint32_t n_parts,

@@ -802,6 +802,41 @@ cudaError_t launch_decode(const DecodeParams &p, DecodeKernel kern, bml_dtype dt
     }
 }
 
+namespace {
+
+// parts [n_parts][n_rows] (m, l) and [n_parts][n_rows][head_dim] o; part i
+// weighs c_i 2^(m_i - M) l_i
+__global__ void merge_counted_kernel(const float *__restrict__ m, const float *__restrict__ l,
+                                     const float *__restrict__ o, uint32_t n_parts, float c0, float c1,
+                                     uint32_t n_rows, uint32_t head_dim, float *__restrict__ out) {
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (size_t)n_rows * head_dim) return;
+    const uint32_t row = (uint32_t)(idx / head_dim), dd = (uint32_t)(idx % head_dim);
+    float M = -INFINITY;
+    for (uint32_t i = 0; i < n_parts; ++i) M = fmaxf(M, m[(size_t)i * n_rows + row]);
+    float L = 0.f, O = 0.f;
+    for (uint32_t i = 0; i < n_parts; ++i) {
+        const float mi = m[(size_t)i * n_rows + row];
+        const float f = mi == -INFINITY ? 0.f : (i == 0 ? c0 : c1) * fast_exp2(mi - M) * l[(size_t)i * n_rows + row];
+        L += f;
+        O += o[((size_t)i * n_rows + row) * head_dim + dd] * f;
+    }
+    out[idx] = O / L;
+}
+
+}  // namespace
+
+cudaError_t launch_merge_counted(const float *m, const float *l, const float *o, uint32_t n_parts,
+                                 const float *counts, uint32_t n_rows, uint32_t head_dim, float *out,
+                                 cudaStream_t stream) {
+    if (n_parts == 0 || n_parts > 2) return cudaErrorInvalidValue;
+    const size_t total = (size_t)n_rows * head_dim;
+    if (total == 0) return cudaSuccess;
+    merge_counted_kernel<<<(unsigned)((total + 255) / 256), 256, 0, stream>>>(
+        m, l, o, n_parts, counts[0], n_parts > 1 ? counts[1] : 0.f, n_rows, head_dim, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_merge_lse(const float *m, const float *l, const float *o, uint32_t n_parts,
                              uint32_t n_rows, uint32_t head_dim, float *out, cudaStream_t stream) {
     const size_t total = (size_t)n_rows * head_dim;

@@ -128,6 +128,12 @@ cudaError_t launch_slot_merge(const DecodeParams &p, uint32_t head_dim, cudaStre
 // launch_slot_merge instead of by its last CTA.
 constexpr uint32_t kInKernelMergeMaxSlots = 8;
 
+// merge_lse with each part's weight multiplied by counts[i] (at most 2
+// parts): the ring-wrap decode's slots visited c+1 and c times.
+cudaError_t launch_merge_counted(const float *m, const float *l, const float *o, uint32_t n_parts,
+                                 const float *counts, uint32_t n_rows, uint32_t head_dim, float *out,
+                                 cudaStream_t stream);
+
 cudaError_t launch_merge_lse(const float *m, const float *l, const float *o, uint32_t n_parts,
                              uint32_t n_rows, uint32_t head_dim, float *out,
                              cudaStream_t stream);

@@ -155,14 +155,16 @@ class HashConsedKV:
         return q
 
     def attention(self, q: torch.Tensor, layer: int, pos: int, scale: float = -1.0,
-                  out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, stream=None, wrap_compat: bool = False) -> torch.Tensor:
         """The attention block of forward_layer_cached (gguf_compiler.rs:
         1008-1050) for the token at `pos`: q [n_heads, head_dim] f32 CUDA
-        tensor -> [n_heads, head_dim] f32."""
+        tensor -> [n_heads, head_dim] f32.  pos >= max_seq_len is refused
+        unless wrap_compat, which reproduces the reference's loop over
+        positions 0..pos read through slot p % max_seq_len (kv_cache.rs:83)."""
         _need(q, "q", torch.float32)
         n_heads = q.numel() // self.head_dim
         if out is None:
             out = torch.empty(n_heads, self.head_dim, dtype=torch.float32, device=q.device)
-        L.call("bml_attn_decode", self._h, layer, pos, n_heads, float(scale), _ptr(q), _ptr(out),
-               _stream(stream))
+        L.call("bml_attn_decode_wrap" if wrap_compat else "bml_attn_decode", self._h, layer, pos, n_heads,
+               float(scale), _ptr(q), _ptr(out), _stream(stream))
         return out

@@ -152,12 +152,28 @@ bml_status bml_kv_append_rope(bml_kv *kv, uint32_t layer, uint32_t pos,
 /* The attention block of forward_layer_cached for the token at position
  * pos: every q head attends over K/V positions [0, pos] of `layer`
  * (causal), softmax, P.V.  q_dev: [n_heads][head_dim] f32, out_dev:
- * [n_heads][head_dim] f32.  pos must be < max_seq_len (the reference's ring
- * wrap, kv_cache.rs:83, is not reproduced).  Uses the handle's own scratch,
- * so calls on one handle must not overlap in time.  Asynchronous. */
+ * [n_heads][head_dim] f32.  pos must be < max_seq_len (for the reference's
+ * ring wrap past max_seq_len, kv_cache.rs:83, use bml_attn_decode_wrap).
+ * Uses the handle's own scratch, so calls on one handle must not overlap in
+ * time.  Asynchronous. */
 bml_status bml_attn_decode(bml_kv *kv, uint32_t layer, uint32_t pos,
                            uint32_t n_heads, float scale, const float *q_dev,
                            float *out_dev, void *stream);
+
+/* bml_attn_decode for any pos, with the reference's behaviour past the end
+ * of the ring: its loop (gguf_compiler.rs:1026-1049) runs over positions
+ * 0..pos and reads each through slot p % max_seq_len (kv_cache.rs:83), so
+ * once pos >= max_seq_len every slot enters the softmax floor(n / M) or
+ * floor(n / M) + 1 times (n = pos + 1, M = max_seq_len; the extra visit for
+ * slots below n % M).  Computed as attention over the M slots with each
+ * slot's weight scaled by its visit count: two KV-split partials merged
+ * with the counts.  pos < max_seq_len is bml_attn_decode itself.  Uses the
+ * handle's own scratch (allocated on first use), so calls on one handle
+ * must not overlap in time.  Asynchronous. */
+bml_status bml_attn_decode_wrap(bml_kv *kv, uint32_t layer, uint32_t pos,
+                                uint32_t n_heads, float scale,
+                                const float *q_dev, float *out_dev,
+                                void *stream);
 
 /* One sequence of a batched decode: a contiguous cache
  * [len][n_kv_heads][head_dim] (K and V), whose query token sits at
