@@ -348,6 +348,46 @@ def cpu_decode_sample(workload: str, budget_s: float, threads: int = 0):
     return nbytes / dt / 1e9, threads, f"{desc}, {reps} passes, {dt * 1e3:.1f} ms/pass"
 
 
+def cpu_literal_sample(workload: str, budget_s: float):
+    """The reference's literal access pattern (a heap copy per load_k, and per
+    load_v inside the head_dim loop; f32 cache as HashConsedKV holds it) on
+    one thread, over the first sequence of the workload's sample, as many q
+    heads as the budget allows; returns (GB/s of the whole sequence at the
+    time per head x n_heads, description)."""
+    import numpy as np
+
+    import oracle
+    from bml_b200 import workloads as W
+    if workload == "batched_tinyllama":
+        q, ks, vs = W.batched_tinyllama(n_seqs=1)
+        q1, k, v = q[0], ks[0].astype(np.float32), vs[0].astype(np.float32)
+        nkv, d = 4, 64
+    else:
+        if workload == "longctx":
+            q1, k, v = W.longctx_decode(length=8192)
+        else:
+            q, kk, vv = W.llama3_decode(n_seqs=1)
+            q1, k, v = q[0], kk[0], vv[0]
+
+        def widen(bits):
+            return (np.ascontiguousarray(bits).view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+        k, v = widen(k), widen(v)
+        nkv, d = 8, 128
+    n_heads, L = q1.shape[0], k.shape[0]
+    t0 = time.perf_counter()
+    h = 0
+    while h < n_heads:
+        oracle.attn_decode_literal(q1, k, v, pos=L - 1, heads=(h, h + 1))
+        h += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    per_head = (time.perf_counter() - t0) / h
+    nbytes = W.decode_bytes(L, nkv, d, 2, 1, n_heads)  # bytes of the stored (16-bit) cache
+    return (nbytes / (per_head * n_heads) / 1e9,
+            f"1 thread, sequence 0 ({L} positions), {h} of {n_heads} q heads, "
+            f"{per_head * 1e3:.0f} ms/head")
+
+
 def cpu_prefill_sample(budget_s: float):
     """Oracle on the last 16 query rows of one head group... of the 4x8192
     prefill; returns TFLOP/s (causal pairs actually computed)."""
@@ -487,8 +527,10 @@ def run_b200(args):
     if dist.world == 1 and not args.no_cpu:
         v, thr, desc = cpu_decode_sample(wl, args.cpu_budget * 0.7)
         v1, _, desc1 = cpu_decode_sample(wl, args.cpu_budget * 0.3, threads=1)
+        vl, descl = cpu_literal_sample(wl, min(4.0, args.cpu_budget * 0.2))
         res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
-                               "sample": desc, "value_1core": round(v1, 4), "sample_1core": desc1}
+                               "sample": desc, "value_1core": round(v1, 4), "sample_1core": desc1,
+                               "value_literal": round(vl, 6), "sample_literal": descl}
         if "prefill" in res and "value" in res["prefill"]:
             pv, pthr, pdesc = cpu_prefill_sample(args.cpu_budget / 2)
             res["prefill"]["cpu_baseline"] = {"value": round(pv, 5), "unit": "TFLOP/s", "cores": pthr,
