@@ -37,7 +37,7 @@ constexpr int kGemvThreads = 256;
 constexpr int kColBlocks = 8;                  // 32-column blocks per CTA
 constexpr int kCols = kColBlocks * 32;         // columns per CTA
 constexpr int kRowPhases = kGemvThreads / kColBlocks;  // 32
-constexpr uint64_t kMaxRanges = 64;                   // row ranges of one GEMV
+constexpr uint64_t kMaxRanges = 160;                  // row ranges of one GEMV
 
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
@@ -240,50 +240,65 @@ __device__ __forceinline__ void cp_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// acc += x * (the 32 values of one block at shared address blk)
+// acc[i] += x * (values 2i, 2i+1 of the one block at shared address blk),
+// in packed f32x2 arithmetic (each lane rounds as fmaf does).  A quantized
+// value becomes a float with one byte permute: its byte lane is moved into
+// the low mantissa byte of 2^23 (the float then reads 2^23 + q), and one
+// packed add removes the offset, exactly.
 template <int QT>
-__device__ __forceinline__ void block_fma_smem(const uint8_t *blk, float x, float acc[32]) {
+__device__ __forceinline__ void block_fma_smem(const uint8_t *blk, float x, float2 acc[16]) {
     if constexpr (QT == kGgufQ4_0 || QT == kGgufQ8_0) {
         const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
         const float xs = x * f16_bits_to_f32(h[0]);
+        const float2 xs2 = make_float2(xs, xs);
         if constexpr (QT == kGgufQ4_0) {
+            const float2 off = make_float2(-8388616.0f, -8388616.0f);  // 2^23 + 8
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const uint32_t two = h[1 + i];
+            for (int m = 0; m < 4; ++m) {
+                // quant bytes 4m..4m+3; byte c holds values 2c (low nibble) and 2c+1
+                const uint32_t w = __byte_perm(h[1 + 2 * m], h[2 + 2 * m], 0x5410);
+                const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) acc[4 * i + k] = fmaf(xs, magic_u((two >> (4 * k)) & 15u, 8.0f), acc[4 * i + k]);
+                for (int b = 0; b < 4; ++b) {
+                    const float2 q = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + b)),
+                                                 __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + b)));
+                    acc[4 * m + b] = __ffma2_rn(xs2, __fadd2_rn(q, off), acc[4 * m + b]);
+                }
             }
         } else {
+            const float2 off = make_float2(-8388736.0f, -8388736.0f);  // 2^23 + 128
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const uint32_t two = h[1 + i];
+            for (int m = 0; m < 8; ++m) {
+                // quant bytes 4m..4m+3 (values 4m..4m+3), int8 -> q + 128
+                const uint32_t w = __byte_perm(h[1 + 2 * m], h[2 + 2 * m], 0x5410) ^ 0x80808080u;
 #pragma unroll
-                for (int k = 0; k < 2; ++k)
-                    acc[2 * i + k] = fmaf(xs, magic_u(((two >> (8 * k)) & 255u) ^ 128u, 128.0f), acc[2 * i + k]);
+                for (int b = 0; b < 4; b += 2) {
+                    const float2 q = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440 + b)),
+                                                 __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441 + b)));
+                    acc[2 * m + b / 2] = __ffma2_rn(xs2, __fadd2_rn(q, off), acc[2 * m + b / 2]);
+                }
             }
         }
     } else if constexpr (QT == kGgufF16) {
         const uint4 *q4 = reinterpret_cast<const uint4 *>(blk);
+        const float2 x2 = make_float2(x, x);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const uint4 q = q4[i];
             const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wd[k]));
-                acc[8 * i + 2 * k] = fmaf(x, f.x, acc[8 * i + 2 * k]);
-                acc[8 * i + 2 * k + 1] = fmaf(x, f.y, acc[8 * i + 2 * k + 1]);
-            }
+            for (int k = 0; k < 4; ++k)
+                acc[4 * i + k] = __ffma2_rn(x2, __half22float2(*reinterpret_cast<const __half2 *>(&wd[k])),
+                                            acc[4 * i + k]);
         }
     } else {
         const float4 *f4 = reinterpret_cast<const float4 *>(blk);
+        const float2 x2 = make_float2(x, x);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float4 q = f4[i];
-            acc[4 * i] = fmaf(x, q.x, acc[4 * i]);
-            acc[4 * i + 1] = fmaf(x, q.y, acc[4 * i + 1]);
-            acc[4 * i + 2] = fmaf(x, q.z, acc[4 * i + 2]);
-            acc[4 * i + 3] = fmaf(x, q.w, acc[4 * i + 3]);
+            acc[2 * i] = __ffma2_rn(x2, make_float2(q.x, q.y), acc[2 * i]);
+            acc[2 * i + 1] = __ffma2_rn(x2, make_float2(q.z, q.w), acc[2 * i + 1]);
         }
     }
 }
@@ -330,9 +345,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
         cp_commit();  // one group per stage, empty past the end
     };
 
-    float acc[32];
+    float2 acc[16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 16; ++i) acc[i] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int st = 0; st < kRing - 1; ++st) issue(st);
     for (uint32_t st = 0; st < n_stages; ++st) {
@@ -362,7 +377,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
     // the 8 row phases of each column, summed in f64 in phase order
     float *part = reinterpret_cast<float *>(sm);  // [8][1024]
 #pragma unroll
-    for (int i = 0; i < 32; ++i) part[rp * 1024 + cbl * 32 + i] = acc[i];
+    for (int i = 0; i < 16; ++i) {
+        part[rp * 1024 + cbl * 32 + 2 * i] = acc[i].x;
+        part[rp * 1024 + cbl * 32 + 2 * i + 1] = acc[i].y;
+    }
     __syncthreads();
     for (uint32_t c = tid; c < tile_blocks * 32u; c += kGemvThreads) {
         double sacc = 0.0;
@@ -432,10 +450,10 @@ GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms, b
     pl.staged = staged;
     const uint64_t cols = staged ? (uint64_t)kTileBlocks * 32 : (uint64_t)kCols;
     pl.col_tiles = (n_out + cols - 1) / cols;
-    // enough CTAs for ~4 per SM (the staged kernel fits 3 per SM; the rest
-    // of the grid fills the gaps), at least 64 rows a range, at most
-    // kMaxRanges ranges
-    uint64_t ranges = (4ull * num_sms + pl.col_tiles - 1) / pl.col_tiles;
+    // at most one wave of CTAs at 4 per SM (the staged kernel's limit by
+    // registers and by shared memory: a CTA more would run alone after the
+    // wave), at least 64 rows a range, at most kMaxRanges ranges
+    uint64_t ranges = (4ull * num_sms) / pl.col_tiles;
     const uint64_t by_rows = (pl.rows + 63) / 64;
     if (ranges > by_rows) ranges = by_rows;
     if (ranges > kMaxRanges) ranges = kMaxRanges;

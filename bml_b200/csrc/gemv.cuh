@@ -28,7 +28,7 @@ GemvPlan gemv_plan(uint64_t n_in, uint64_t n_out, uint64_t x_len, int num_sms, b
 // The staged kernel applies: n_out % 256 == 0, W 16-byte aligned, and the
 // data holds the whole n_in x n_out tensor.
 bool gemv_staged_ok(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in, uint64_t n_out);
-// Scratch for the row-range partials: at most 64 ranges of n_out doubles.
+// Scratch for the row-range partials: at most 160 ranges of n_out doubles.
 size_t gemv_workspace_bytes(uint64_t n_out);
 
 // y[j] = sum_i x[i] * W[i*n_out + j] over the tensor's values (see gemv.cu).

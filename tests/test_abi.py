@@ -108,4 +108,4 @@ def test_weight_path_rejects_on_host(L):
     # misaligned F32 weights
     assert lib.bml_matmul_f64(18, 64, L.GGUF_F32, 4, 4, 16, 4, 16, None, 0, None) == L.BML_E_INVALID
     size = C.c_size_t()
-    assert lib.bml_matmul_workspace_size(4096, C.byref(size)) == L.BML_OK and size.value == 64 * 4096 * 8
+    assert lib.bml_matmul_workspace_size(4096, C.byref(size)) == L.BML_OK and size.value == 160 * 4096 * 8
