@@ -24,7 +24,7 @@
 // int-to-float conversion unit in the loop).  The 32 row phases are summed
 // in f64 in a fixed order, and the row ranges (when a tensor needs several
 // CTAs per column range to fill the GPU) go to a workspace in f64 and are
-// summed in range order by a second kernel, so results do not vary between
+// summed in a fixed order by a second kernel, so results do not vary between
 // runs; against the reference's f64 sums they differ by f32 rounding of the
 // terms and partial sums (about 1e-7 of sum |x_i W_ij|).
 #include "gemv.cuh"
@@ -390,13 +390,26 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
     }
 }
 
-__global__ void gemv_reduce_kernel(const double *__restrict__ partial, uint32_t n_ranges, uint64_t n_out,
-                                   double *__restrict__ y) {
-    const uint64_t j = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= n_out) return;
+// y[j] = sum of the row ranges' partials.  A CTA takes 32 columns; warp g
+// sums ranges g, g+8, g+16, ... of them in that order (8 loads in flight per
+// column instead of one), and the 8 group sums are added in group order: a
+// fixed association, so results do not vary between runs.
+__global__ void __launch_bounds__(256) gemv_reduce_kernel(const double *__restrict__ partial, uint32_t n_ranges,
+                                                          uint64_t n_out, double *__restrict__ y) {
+    __shared__ double grp[8][33];
+    const uint32_t c = threadIdx.x & 31, g = threadIdx.x >> 5;
+    const uint64_t j = (uint64_t)blockIdx.x * 32 + c;
     double s = 0.0;
-    for (uint32_t r = 0; r < n_ranges; ++r) s += partial[(uint64_t)r * n_out + j];
-    y[j] = s;
+    if (j < n_out)
+        for (uint32_t r = g; r < n_ranges; r += 8) s += partial[(uint64_t)r * n_out + j];
+    grp[g][c] = s;
+    __syncthreads();
+    if (g == 0 && j < n_out) {
+        double t = grp[0][c];
+#pragma unroll
+        for (int k = 1; k < 8; ++k) t += grp[k][c];
+        y[j] = t;
+    }
 }
 
 }  // namespace
@@ -519,7 +532,7 @@ cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in,
             default: return cudaErrorInvalidValue;
         }
         if (se != cudaSuccess || pl.ranges == 1) return se;
-        gemv_reduce_kernel<<<(unsigned)((n_out + 255) / 256), 256, 0, st>>>(partial, pl.ranges, n_out, y);
+        gemv_reduce_kernel<<<(unsigned)((n_out + 31) / 32), 256, 0, st>>>(partial, pl.ranges, n_out, y);
         return cudaGetLastError();
     }
     switch (gguf_type) {
@@ -531,7 +544,7 @@ cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in,
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || pl.ranges == 1) return e;
-    gemv_reduce_kernel<<<(unsigned)((n_out + 255) / 256), 256, 0, st>>>(partial, pl.ranges, n_out, y);
+    gemv_reduce_kernel<<<(unsigned)((n_out + 31) / 32), 256, 0, st>>>(partial, pl.ranges, n_out, y);
     return cudaGetLastError();
 }
 
