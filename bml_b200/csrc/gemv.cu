@@ -227,10 +227,14 @@ struct StagedCfg {
     static constexpr uint32_t SEG = kTileBlocks * BB;  // bytes of one row of a tile
     static constexpr uint32_t RS_RAW = 18432u / SEG;
     static constexpr uint32_t RS = RS_RAW < 8u ? 8u : (RS_RAW / 8u) * 8u;  // rows per stage
-    static constexpr uint32_t STAGE = RS * SEG;
+    static constexpr uint32_t XOFF = RS * SEG;        // the stage's RS values of x (f64) follow its rows
+    static constexpr uint32_t STAGE = XOFF + RS * 8u;
     static constexpr uint32_t SMEM = kRing * STAGE > 8u * 1024u * 4u ? kRing * STAGE : 8u * 1024u * 4u;
 };
 
+__device__ __forceinline__ void cp8(uint32_t dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp16(uint32_t dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -341,6 +345,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
                 const uint32_t cc = c - rr * seg_chunks;
                 cp16(slot + rr * Cf::SEG + cc * 16u, tile + (rb + rr) * row_bytes + cc * 16u);
             }
+            // the stage's x values ride along: no global load in the compute loop
+            if ((uint32_t)tid < nr) cp8(slot + Cf::XOFF + tid * 8u, x + rb + tid);
         }
         cp_commit();  // one group per stage, empty past the end
     };
@@ -358,16 +364,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
         const uint32_t nr = stage_rows(st);
         if ((uint32_t)cbl < tile_blocks) {
             const uint8_t *slot = sm + (st % kRing) * Cf::STAGE;
+            const double *xst = reinterpret_cast<const double *>(slot + Cf::XOFF);
             constexpr uint32_t kStep = kGemvThreads / kTileBlocks;
             if (nr == Cf::RS) {  // full stage: a fixed trip count, unrolled for independent loads
 #pragma unroll
                 for (uint32_t k = 0; k < Cf::RS / kStep; ++k) {
                     const uint32_t rr = rp + k * kStep;
-                    block_fma_smem<QT>(slot + rr * Cf::SEG + cbl * Cf::BB, (float)__ldg(x + rb + rr), acc);
+                    block_fma_smem<QT>(slot + rr * Cf::SEG + cbl * Cf::BB, (float)xst[rr], acc);
                 }
             } else {
                 for (uint32_t rr = rp; rr < nr; rr += kStep)
-                    block_fma_smem<QT>(slot + rr * Cf::SEG + cbl * Cf::BB, (float)__ldg(x + rb + rr), acc);
+                    block_fma_smem<QT>(slot + rr * Cf::SEG + cbl * Cf::BB, (float)xst[rr], acc);
             }
         }
         __syncthreads();  // the slot is refilled next iteration
