@@ -308,7 +308,7 @@ __device__ __forceinline__ void block_fma_smem(const uint8_t *blk, float x, floa
 }
 
 template <int QT>
-__global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t *__restrict__ w, uint64_t n_out,
+__global__ void __launch_bounds__(kGemvThreads, 4) gemv_staged_kernel(const uint8_t *__restrict__ w, uint64_t n_out,
                                                                    uint64_t rows, uint64_t rows_per_range,
                                                                    const double *__restrict__ x,
                                                                    double *__restrict__ dst) {
@@ -322,7 +322,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
     // blocks of this tile: a multiple of 8 (n_out % 256 == 0)
     const uint32_t tile_blocks = (uint32_t)(n_cb - cb0 < (uint64_t)kTileBlocks ? n_cb - cb0 : (uint64_t)kTileBlocks);
     const uint32_t seg_chunks = tile_blocks * Cf::BB / 16u;  // <= 256
-    const float inv_seg = 1.0f / (float)seg_chunks;
+    // this thread's chunks of a stage: chunk tid, tid + 256, ... as (row,
+    // chunk in row), stepped without a division per chunk
+    const uint32_t rr0 = (uint32_t)tid / seg_chunks, cc0 = (uint32_t)tid % seg_chunks;
+    const uint32_t d_rr = (uint32_t)kGemvThreads / seg_chunks, d_cc = (uint32_t)kGemvThreads % seg_chunks;
     const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_range;
     const uint64_t r1 = min(r0 + rows_per_range, rows);
     const uint32_t n_stages = (uint32_t)((r1 - r0 + Cf::RS - 1) / Cf::RS);
@@ -338,12 +341,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_staged_kernel(const uint8_t
             const uint64_t rb = r0 + (uint64_t)st * Cf::RS;
             const uint32_t nr = stage_rows(st);
             const uint32_t slot = smem0 + (st % kRing) * Cf::STAGE;
-            for (uint32_t c = tid; c < nr * seg_chunks; c += kGemvThreads) {
-                // c / seg_chunks without an integer division: c < 2^13 and
-                // (c + 1/2) / seg_chunks stays at least 1/512 from an integer
-                const uint32_t rr = (uint32_t)(((float)c + 0.5f) * inv_seg);
-                const uint32_t cc = c - rr * seg_chunks;
+            uint32_t rr = rr0, cc = cc0;
+            while (rr < nr) {
                 cp16(slot + rr * Cf::SEG + cc * 16u, tile + (rb + rr) * row_bytes + cc * 16u);
+                rr += d_rr;
+                cc += d_cc;
+                if (cc >= seg_chunks) {
+                    cc -= seg_chunks;
+                    ++rr;
+                }
             }
             // the stage's x values ride along: no global load in the compute loop
             if ((uint32_t)tid < nr) cp8(slot + Cf::XOFF + tid * 8u, x + rb + tid);
