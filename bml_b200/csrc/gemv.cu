@@ -215,9 +215,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const uint8_t *__res
 // aligned and the data holds the whole tensor (rows are then 16-byte
 // aligned runs of n_out/32 blocks).  The direct kernel above has each
 // thread wait on its own scattered 2-byte loads, one row after another;
-// here 256 threads keep three stages of whole row segments in flight.
-// Thread t owns 32-column block t % 32 of the tile and rows t / 32 (mod 8)
-// of each stage.
+// here 256 threads keep three stages of whole row segments (and the x
+// values of those rows) in flight.  Thread t owns 32-column block t % 32 of
+// the tile and rows t / 32 (mod 8) of each stage.
 constexpr int kTileBlocks = 32;
 constexpr int kRing = 3;
 
