@@ -599,24 +599,30 @@ def run_longctx(args, dist, peaks, res):
     step_bytes = decode_step_bytes(batch, H)
     total = dist.sum(step_bytes)
     gbs = total * args.steps / (ms * 1e-3) / 1e9
-    kfn = lambda: bml_b200.decode_partial(q, batch, workspace=ws)  # noqa: E731
+    if dist.world > 1:
+        kfn = lambda: bml_b200.decode_partial(q, batch, workspace=ws)  # noqa: E731
+    else:  # what the one-GPU step runs
+        kfn = lambda: bml_b200.decode_batched(q, batch, out=merged, workspace=ws)  # noqa: E731
     kms = kernel_ms(kfn)
     ach = step_bytes / (kms * 1e-3) / 1e9
     hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
     res.update({"metric": DECODE_METRIC, "value": round(gbs, 1), "unit": "GB/s",
                 "ms_per_step": round(ms / args.steps, 5), "scaling": "strong", "dtype": "f32 (bf16 KV)",
                 "config": {"workload": "longctx", "context": total_len, "n_heads": H, "n_kv_heads": Hkv,
-                           "head_dim": d, "split": f"KV length over {dist.world} GPUs, NCCL all_gather of "
-                                                   "(m, l, o) + LSE merge",
-                           "l2": "256 MiB of KV per step on 1 GPU"},
+                           "head_dim": d,
+                           "split": (f"KV length over {dist.world} GPUs, NCCL all_gather of (m, l, o) + LSE merge"
+                                     if dist.world > 1 else "one GPU: the whole sequence, plain decode"),
+                           "l2": "512 MiB of KV (K + V) per step on 1 GPU"},
                 "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                              "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
                              "traffic": profile_traffic("decode_longctx.txt"),
                              "kernel": decode_kernel_name(torch.bfloat16, d, Hkv, H // Hkv) + " + slot_merge_kernel",
                              "kernel_ms": round(kms, 5)},
                 # per step: decode_bulk_kernel + slot_merge_kernel (the
-                # partials) + merge_lse_packed_kernel; NCCL's all-gather between
-                "clocks": clocks, "gpu_launches": 3 * args.steps})
+                # partials) + merge_lse_packed_kernel, NCCL's all-gather
+                # between; on one GPU the plain decode (its slot merge gives
+                # the output)
+                "clocks": clocks, "gpu_launches": (3 if dist.world > 1 else 2) * args.steps})
     if dist.world == 1 and not args.no_cpu:
         v, thr, desc = cpu_decode_sample("longctx", args.cpu_budget)
         res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",

@@ -81,6 +81,11 @@ class KVSplitDecode:
 
     def __call__(self, q, batch, workspace=None, out=None):
         torch = self._torch
+        if self.world == 1 and self.partial_fn is None and self.merge_fn is None:
+            # one rank holds the whole sequence: the plain decode, whose slot
+            # merge already yields the final output (no partial, no merge)
+            from .attention import decode_batched
+            return decode_batched(q, batch, out=out, workspace=workspace)
         n_seqs = q.shape[0]
         n_rows = n_seqs * self.n_heads
         packed, gathered = self._buffers(n_rows)

@@ -310,3 +310,23 @@ def test_workspace_shared_by_calls_of_different_shapes(cuda):
                                           workspace=ws).cpu().numpy()
             assert np.abs(got - want).max() < TOL
     ws.check()
+
+
+def test_kv_split_decode_one_rank(cuda):
+    """KVSplitDecode with a single rank runs the plain decode (no partial,
+    no merge); a 5000-position bf16 sequence against the oracle."""
+    import bml_b200
+    from bml_b200 import sharding
+    rng = np.random.default_rng(41)
+    L, n_kv, d, H = 5000, 8, 128, 32
+    q = rng.standard_normal((1, H, d), dtype=np.float32)
+    kf = rng.standard_normal((L, n_kv, d), dtype=np.float32)
+    vf = rng.standard_normal((L, n_kv, d), dtype=np.float32)
+    k = (kf.view(np.uint32) >> 16).astype(np.uint16)  # bf16 by truncation
+    v = (vf.view(np.uint32) >> 16).astype(np.uint16)
+    batch = bml_b200.SeqBatch([to_dev(k, oracle.BF16)], [to_dev(v, oracle.BF16)])
+    ws = bml_b200.Workspace(torch.device("cuda")).ensure(1, H, d)
+    step = sharding.KVSplitDecode(None, 1, H, d, torch.device("cuda"))
+    got = step(to_dev(q), batch, ws).cpu().numpy()
+    want = oracle.attn_decode_batched(q, [k], [v], dtype=oracle.BF16)
+    assert np.abs(got - want).max() < TOL
