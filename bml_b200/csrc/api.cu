@@ -587,7 +587,7 @@ BML_API bml_status bml_attn_decode(bml_kv *kv, uint32_t layer, uint32_t pos, uin
     if (!kv) return fail(BML_E_INVALID, "bml_attn_decode: null handle");
     if (layer >= kv->desc.n_layers) return fail(BML_E_INVALID, "bml_attn_decode: layer %u", layer);
     if (pos >= kv->desc.max_seq_len)
-        return fail(BML_E_INVALID, "bml_attn_decode: pos %u >= max_seq_len %u (ring wrap not reproduced)", pos,
+        return fail(BML_E_INVALID, "bml_attn_decode: pos %u >= max_seq_len %u (the ring wrap is bml_attn_decode_wrap)", pos,
                     kv->desc.max_seq_len);
     bml_status st = check_decode_shape(n_heads, kv->desc.n_kv_heads, kv->desc.head_dim, kv->desc.dtype,
                                        "bml_attn_decode");
