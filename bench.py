@@ -16,7 +16,8 @@ is already resident in HBM.  Workloads (--workload):
   longctx                  one 131072-position sequence (Llama-3 heads,
                            bf16) split along its KV length over the GPUs;
                            per-GPU (m, l, o) partials all-gathered over
-                           NCCL and merged ("strong").
+                           NCCL and merged ("strong"); one GPU runs the
+                           plain decode of the whole sequence.
   llama3_prefill           causal prefill 4 x 8192, 32/8 heads, d=128,
                            bf16 operands (TFLOP/s of 4*d*H*causal pairs).
   gemv                     the projections of Llama-3-8B layers (q, k, v, o
