@@ -481,9 +481,10 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
             // run time (measured: 4-12 per SM within 3% on batches; fewer
             // is better for one long sequence, where the partials' traffic
             // and merge weigh more), and at least 8 tiles (measured on a
-            // small batch, 147 MB of KV: 8 tiles 4.6% faster than 4, whose
-            // extra slots cost more in the merge than the finer split
-            // gains).  Each chunk leaves one partial slot per
+            // small batch, 147 MB of KV: a minimum of 8 tiles beats 4, whose
+            // extra slots cost more in the merge than the finer split gains,
+            // and 12 or 16, which leave too few chunks to balance; likewise
+            // on the 32-request serving loop).  Each chunk leaves one partial slot per
             // warp of a kv head (8 / n_kv), so C grows until the slots fit
             // the workspace and a sequence has at most 512 of them.
             const uint32_t nph = 8u / n_kv;
