@@ -19,7 +19,9 @@ is already resident in HBM.  Workloads (--workload):
                            NCCL and merged ("strong"); one GPU runs the
                            plain decode of the whole sequence.
   llama3_prefill           causal prefill 4 x 8192, 32/8 heads, d=128,
-                           bf16 operands (TFLOP/s of 4*d*H*causal pairs).
+                           bf16 operands (TFLOP/s of 4*d*H*causal pairs);
+                           the 32 (sequence, kv-head group) units are dealt
+                           over the GPUs ("strong", no collective).
   gemv                     the projections of Llama-3-8B layers (q, k, v, o
                            4096x4096/1024; gate, up 4096x14336; down
                            14336x4096) as Q4_0 tensors read in place by
@@ -40,8 +42,10 @@ is already resident in HBM.  Workloads (--workload):
                            the longest request leaves and a new one joins.
                            Metric: HBM GB/s of algorithmic bytes ("weak").
 
-The default decode line also carries a "prefill" object measured in the
-same run on the llama3_prefill workload.
+The default decode line also carries, measured in the same run at the same
+GPU count, a "prefill" object (llama3_prefill split by (sequence x kv-head
+group), strong), a "batched_tinyllama" object (strong) and a "longctx"
+object (strong).
 
 --impl reference times the CPU restatement of the reference's attention
 (oracle/, the reference is Rust and cannot be built here) on the host cores
@@ -414,17 +418,42 @@ def cpu_prefill_sample(budget_s: float):
 # ---------------------------------------------------------------------------
 # arms
 # ---------------------------------------------------------------------------
+def prefill_units(rank: int, world: int, n: int = 4, n_kv: int = 8):
+    """This rank's share of a prefill of n sequences with n_kv kv heads, cut
+    into n * n_kv (sequence, kv-head group) units dealt out in contiguous
+    runs: (first sequence, sequences, first kv head, kv heads).  For world
+    in 1, 2, 4, 8 and 4 x 8 units a share is whole sequences or a run of kv
+    heads of one sequence, so it is one launch."""
+    units = n * n_kv
+    if units % world:
+        raise SystemExit(f"{units} prefill units do not split over {world} ranks")
+    per = units // world
+    u0 = rank * per
+    if per >= n_kv:
+        if per % n_kv or u0 % n_kv:
+            raise SystemExit("prefill share is not whole sequences")
+        return u0 // n_kv, per // n_kv, 0, n_kv
+    if n_kv % per:
+        raise SystemExit("prefill share straddles sequences")
+    return u0 // n_kv, 1, u0 % n_kv, per
+
+
 def run_prefill(dev, steps, warmup, dist, peaks, n=4, S=8192):
+    """Causal prefill of n x S tokens (Llama-3-8B heads) split over the ranks
+    by (sequence x kv-head group) with no collective ("strong": the total
+    work is fixed).  Each rank holds the q/k/v of its own units only."""
     import torch
 
     import bml_b200
     from bml_b200 import workloads as W
-    gen = torch.Generator(device=dev).manual_seed(3 + 1000 * dist.rank)
     H, Hkv, d = 32, 8, 128
-    q = gen_normal((n, S, H, d), torch.bfloat16, dev, gen)
-    k = gen_normal((n, S, Hkv, d), torch.bfloat16, dev, gen)
-    v = gen_normal((n, S, Hkv, d), torch.bfloat16, dev, gen)
-    out = torch.empty(n, S, H, d, dtype=torch.float32, device=dev)
+    G = H // Hkv
+    s0, ns, h0, nh = prefill_units(dist.rank, dist.world, n, Hkv)
+    gen = torch.Generator(device=dev).manual_seed(3 + 1000 * dist.rank)
+    q = gen_normal((ns, S, nh * G, d), torch.bfloat16, dev, gen)
+    k = gen_normal((ns, S, nh, d), torch.bfloat16, dev, gen)
+    v = gen_normal((ns, S, nh, d), torch.bfloat16, dev, gen)
+    out = torch.empty(ns, S, nh * G, d, dtype=torch.float32, device=dev)
     fn = lambda: bml_b200.prefill(q, k, v, out=out)  # noqa: E731
     try:
         fn()
@@ -432,19 +461,67 @@ def run_prefill(dev, steps, warmup, dist, peaks, n=4, S=8192):
     except bml_b200.BmlUnsupported as e:
         return {"unavailable": str(e)}
     ms, clocks = timed_loop(fn, steps, warmup, dist, dist.local)
-    flops = W.prefill_flops(n, S, H, d)
-    tflops = dist.world * flops * steps / (ms * 1e-3) / 1e12
+    flops_total = W.prefill_flops(n, S, H, d)
+    flops_mine = W.prefill_flops(ns, S, nh * G, d)
+    tflops = flops_total * steps / (ms * 1e-3) / 1e12
     kms = kernel_ms(fn, 10)
-    ach = flops / (kms * 1e-3) / 1e12
+    ach = flops_mine / (kms * 1e-3) / 1e12
     peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    peak_s = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    loop_rank = flops_mine * steps / (ms * 1e-3) / 1e12
     return {"metric": "causal prefill TFLOP/s", "value": round(tflops, 2), "unit": "TFLOP/s",
-            "ms_per_step": round(ms / steps, 4), "steps": steps,
+            "ms_per_step": round(ms / steps, 4), "steps": steps, "scaling": "strong",
             "config": {"workload": "llama3_prefill", "n_seqs": n, "seq_len": S, "n_heads": H,
-                       "n_kv_heads": Hkv, "head_dim": d, "causal": True, "dtype": "bf16"},
+                       "n_kv_heads": Hkv, "head_dim": d, "causal": True, "dtype": "bf16",
+                       "split": f"{n * Hkv} (sequence, kv-head group) units over {dist.world} GPU(s), no collective",
+                       "rank0_share": {"first_seq": s0, "seqs": ns, "first_kv_head": h0, "kv_heads": nh}},
             "roofline": {"bound": "tensor", "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(ach / peak, 4), "frac_spec": round(ach / SPEC_PEAKS["bf16_tflops"], 4),
-                         "traffic": profile_traffic("prefill_tcgen05_llama3.txt")},
+                         "peak_kind": "measured cuBLAS bf16 burst (kernel timed alone, 10 launches)",
+                         "loop_per_gpu": round(loop_rank, 2),
+                         "loop_frac_sustained": round(loop_rank / peak_s, 4),
+                         "traffic": profile_traffic("prefill_tcgen05_llama3.txt") if dist.world == 1 else None,
+                         "kernel": "prefill_kernel", "kernel_ms": round(kms, 4),
+                         "algorithmic_flops_per_launch": flops_mine},
             "clocks": clocks}
+
+
+def run_tinyllama_obj(dev, steps, warmup, dist, peaks, cpu_budget):
+    """The 64-sequence ragged TinyLlama-shaped batch (U[128,4096], f16 KV),
+    sequences dealt over the ranks by longest-processing-time ("strong", no
+    collective)."""
+    import torch
+
+    import bml_b200
+    q, batch, H, _ = build_batched_tinyllama(dev, dist.rank, dist.world)
+    ws = bml_b200.Workspace(dev).ensure(len(batch), H, batch.head_dim)
+    out = torch.empty_like(q)
+    fn = lambda: bml_b200.decode_batched(q, batch, out=out, workspace=ws)  # noqa: E731
+    fn()
+    torch.cuda.synchronize()
+    ms, clocks = timed_loop(fn, steps, warmup, dist, dist.local)
+    step_bytes = decode_step_bytes(batch, H)
+    total = dist.sum(step_bytes)
+    kms = kernel_ms(fn)
+    ws.check()
+    ach = step_bytes / (kms * 1e-3) / 1e9
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    res = {"metric": "batched decode HBM GB/s", "value": round(total * steps / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "ms_per_step": round(ms / steps, 5), "steps": steps, "scaling": "strong",
+           "config": {"workload": "batched_tinyllama", "n_seqs": 64, "n_seqs_rank0": len(batch),
+                      "lengths": "U[128,4096] seed 2", "n_heads": H, "n_kv_heads": 4, "head_dim": 64,
+                      "kv_dtype": "f16", "sharding": f"LPT over {dist.world} GPU(s), no collective",
+                      "l2": "147 MB of KV per step (all ranks) vs 126 MB L2"},
+           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
+                        "traffic": profile_traffic("decode_batched_tinyllama.txt") if dist.world == 1 else None,
+                        "kernel": "decode_bulk_kernel", "kernel_ms": round(kms, 5),
+                        "algorithmic_bytes_per_launch": step_bytes},
+           "clocks": clocks}
+    if dist.world == 1 and cpu_budget > 0:
+        v, thr, desc = cpu_decode_sample("batched_tinyllama", cpu_budget)
+        res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port", "sample": desc}
+    return res
 
 
 def run_b200(args):
@@ -459,38 +536,34 @@ def run_b200(args):
            "vs_baseline": None, "data": "synthetic: seeded N(0,1) on the device (torch generator)",
            "peak_source": f"{peak_kind} ({PEAKS_PATH if peak_kind == 'measured' else 'fallback'})"}
     wl = args.workload
+    cpu = 0.0 if args.no_cpu or dist.world > 1 else args.cpu_budget
     if wl == "llama3_prefill":
         pre = run_prefill(dev, args.steps, args.warmup, dist, peaks, args.prefill_n, args.prefill_s)
         res.update(pre)
-        res.update({"metric": DECODE_METRIC, "dtype": "bf16", "scaling": "weak", "gpu_launches": args.steps})
+        res.update({"metric": DECODE_METRIC, "dtype": "bf16", "gpu_launches": args.steps})
         emit(res, dist)
         return
-    if wl == "llama3_decode":
-        q, batch, H = build_llama3_decode(dev, 3 + 1000 * dist.rank)
-        scaling = "weak"
-        cfg = {"workload": "llama3_decode", "n_seqs_per_gpu": len(batch), "context": 8192, "n_heads": H,
-               "n_kv_heads": 8, "head_dim": 128, "kv_dtype": "bf16",
-               "l2": "inputs larger than L2 (1 GiB of KV per step vs 126 MB)"}
-        dtype = "f32 (bf16 KV)"
-    elif wl == "batched_tinyllama":
-        q, batch, H, _ = build_batched_tinyllama(dev, dist.rank, dist.world)
-        scaling = "strong"
-        cfg = {"workload": "batched_tinyllama", "n_seqs": 64, "lengths": "U[128,4096] seed 2",
-               "n_heads": H, "n_kv_heads": 4, "head_dim": 64, "kv_dtype": "f16",
-               "sharding": "LPT over GPUs, no collective",
-               "l2": "147 MB of KV per step > 126 MB L2"}
-        dtype = "f32 (f16 KV)"
-    elif wl == "longctx":
+    if wl == "batched_tinyllama":
+        obj = run_tinyllama_obj(dev, args.steps, args.warmup, dist, peaks, cpu)
+        res.update(obj)
+        res.update({"metric": DECODE_METRIC, "dtype": "f32 (f16 KV)", "gpu_launches": args.steps})
+        emit(res, dist)
+        return
+    if wl == "longctx":
         return run_longctx(args, dist, peaks, res)
-    elif wl == "serving":
+    if wl == "serving":
         return run_serving(args, dist, peaks, res)
-    elif wl == "gemv":
+    if wl == "gemv":
         return run_gemv(args, dist, peaks, res)
-    elif wl == "gguf_load":
+    if wl == "gguf_load":
         return run_gguf_load(args, dist, peaks, res)
-    else:
+    if wl != "llama3_decode":
         raise SystemExit(f"unknown workload {wl}")
 
+    q, batch, H = build_llama3_decode(dev, 3 + 1000 * dist.rank)
+    cfg = {"workload": "llama3_decode", "n_seqs_per_gpu": len(batch), "context": 8192, "n_heads": H,
+           "n_kv_heads": 8, "head_dim": 128, "kv_dtype": "bf16",
+           "l2": "inputs larger than L2 (1 GiB of KV per step vs 126 MB)"}
     ws = bml_b200.Workspace(dev).ensure(len(batch), H, batch.head_dim)
     out = torch.empty_like(q)
     fn = lambda: bml_b200.decode_batched(q, batch, out=out, workspace=ws)  # noqa: E731
@@ -509,22 +582,18 @@ def run_b200(args):
 
     res.update({
         "metric": DECODE_METRIC, "value": round(gbs, 1), "unit": "GB/s",
-        "ms_per_step": round(ms / args.steps, 5), "scaling": scaling, "dtype": dtype, "config": cfg,
+        "ms_per_step": round(ms / args.steps, 5), "scaling": "weak", "dtype": "f32 (bf16 KV)", "config": cfg,
         "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
-                     "traffic": profile_traffic(f"decode_{wl}.txt"),
-                     "kernel": decode_kernel_name(batch.dtype, batch.head_dim, batch.n_kv, H // batch.n_kv)
-                     + " + slot_merge_kernel",
+                     "traffic": profile_traffic("decode_llama3_decode.txt"),
+                     "kernel": decode_kernel_name(batch.dtype, batch.head_dim, batch.n_kv, H // batch.n_kv),
                      "kernel_ms": round(kms, 5),
                      "algorithmic_bytes_per_launch": step_bytes},
-        # per step: decode_bulk_kernel + slot_merge_kernel (every sequence of
-        # these batches spans several chunks)
-        "clocks": clocks, "e2e": e2e, "gpu_launches": 2 * args.steps,
+        # per step: one decode_bulk_kernel (partials merged in the same launch)
+        "clocks": clocks, "e2e": e2e, "gpu_launches": args.steps,
     })
-    if not args.no_prefill and wl == "llama3_decode":
-        pre = run_prefill(dev, max(3, args.prefill_steps), 3, dist, peaks)
-        res["prefill"] = pre
-        res["gpu_launches"] += pre.get("steps", 0)
+    del q, batch, ws, out
+    torch.cuda.empty_cache()
     if dist.world == 1 and not args.no_cpu:
         v, thr, desc = cpu_decode_sample(wl, args.cpu_budget * 0.7)
         v1, _, desc1 = cpu_decode_sample(wl, args.cpu_budget * 0.3, threads=1)
@@ -532,10 +601,24 @@ def run_b200(args):
         res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
                                "sample": desc, "value_1core": round(v1, 4), "sample_1core": desc1,
                                "value_literal": round(vl, 6), "sample_literal": descl}
-        if "prefill" in res and "value" in res["prefill"]:
+    if not args.no_prefill:
+        pre = run_prefill(dev, max(3, args.prefill_steps), 3, dist, peaks)
+        if dist.world == 1 and not args.no_cpu and "value" in pre:
             pv, pthr, pdesc = cpu_prefill_sample(args.cpu_budget / 2)
-            res["prefill"]["cpu_baseline"] = {"value": round(pv, 5), "unit": "TFLOP/s", "cores": pthr,
-                                              "kind": "port", "sample": pdesc}
+            pre["cpu_baseline"] = {"value": round(pv, 5), "unit": "TFLOP/s", "cores": pthr, "kind": "port",
+                                   "sample": pdesc}
+        res["prefill"] = pre
+        res["gpu_launches"] += pre.get("steps", 0)
+        torch.cuda.empty_cache()
+    if not args.no_sub:
+        sub_steps = max(args.steps, args.sub_steps)
+        tiny = run_tinyllama_obj(dev, sub_steps, max(3, args.warmup), dist, peaks, cpu / 2)
+        res["batched_tinyllama"] = tiny
+        res["gpu_launches"] += sub_steps
+        torch.cuda.empty_cache()
+        lc = run_longctx_obj(dev, sub_steps, max(3, args.warmup), dist, peaks, cpu / 2)
+        res["gpu_launches"] += sub_steps * lc.pop("launches_per_step")
+        res["longctx"] = lc
     emit(res, dist)
 
 
@@ -575,12 +658,15 @@ def e2e_decode(q, batch, ws, args, dist, step_bytes):
             "steps": n, "ms_per_step": round(ms / n, 5)}
 
 
-def run_longctx(args, dist, peaks, res):
+def run_longctx_obj(dev, steps, warmup, dist, peaks, cpu_budget):
+    """One 131072-position sequence (Llama-3-8B heads, bf16 KV) split along
+    its KV length over the ranks; per-rank (m, l, o) partials exchanged and
+    merged ("strong").  One GPU runs the plain decode of the whole
+    sequence."""
     import torch
 
     import bml_b200
     from bml_b200 import sharding
-    dev = dist.device
     total_len, H, Hkv, d = 131072, 32, 8, 128
     lo, hi = sharding.kv_split_ranges(total_len, dist.world)[dist.rank]
     gen = torch.Generator(device=dev).manual_seed(4)
@@ -596,38 +682,46 @@ def run_longctx(args, dist, peaks, res):
     fn = lambda: step(q, batch, ws, out=merged)  # noqa: E731
     fn()
     torch.cuda.synchronize()
-    ms, clocks = timed_loop(fn, args.steps, args.warmup, dist, dist.local)
+    ms, clocks = timed_loop(fn, steps, warmup, dist, dist.local)
     step_bytes = decode_step_bytes(batch, H)
     total = dist.sum(step_bytes)
-    gbs = total * args.steps / (ms * 1e-3) / 1e9
+    gbs = total * steps / (ms * 1e-3) / 1e9
     if dist.world > 1:
         kfn = lambda: bml_b200.decode_partial(q, batch, workspace=ws)  # noqa: E731
     else:  # what the one-GPU step runs
         kfn = lambda: bml_b200.decode_batched(q, batch, out=merged, workspace=ws)  # noqa: E731
     kms = kernel_ms(kfn)
+    ws.check()
     ach = step_bytes / (kms * 1e-3) / 1e9
     hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
-    res.update({"metric": DECODE_METRIC, "value": round(gbs, 1), "unit": "GB/s",
-                "ms_per_step": round(ms / args.steps, 5), "scaling": "strong", "dtype": "f32 (bf16 KV)",
-                "config": {"workload": "longctx", "context": total_len, "n_heads": H, "n_kv_heads": Hkv,
-                           "head_dim": d,
-                           "split": (f"KV length over {dist.world} GPUs, NCCL all_gather of (m, l, o) + LSE merge"
-                                     if dist.world > 1 else "one GPU: the whole sequence, plain decode"),
-                           "l2": "512 MiB of KV (K + V) per step on 1 GPU"},
-                "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
-                             "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
-                             "traffic": profile_traffic("decode_longctx.txt"),
-                             "kernel": decode_kernel_name(torch.bfloat16, d, Hkv, H // Hkv) + " + slot_merge_kernel",
-                             "kernel_ms": round(kms, 5)},
-                # per step: decode_bulk_kernel + slot_merge_kernel (the
-                # partials) + merge_lse_packed_kernel, NCCL's all-gather
-                # between; on one GPU the plain decode (its slot merge gives
-                # the output)
-                "clocks": clocks, "gpu_launches": (3 if dist.world > 1 else 2) * args.steps})
-    if dist.world == 1 and not args.no_cpu:
-        v, thr, desc = cpu_decode_sample("longctx", args.cpu_budget)
-        res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port",
-                               "sample": desc}
+    res = {"metric": "sequence-split decode HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
+           "ms_per_step": round(ms / steps, 5), "steps": steps, "scaling": "strong",
+           "config": {"workload": "longctx", "context": total_len, "n_heads": H, "n_kv_heads": Hkv,
+                      "head_dim": d, "kv_dtype": "bf16",
+                      "split": (f"KV length over {dist.world} GPUs, NCCL all_gather of (m, l, o) + LSE merge"
+                                if dist.world > 1 else "one GPU: the whole sequence, plain decode"),
+                      "l2": "512 MiB of KV (K + V) per step, all ranks"},
+           "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
+                        "traffic": profile_traffic("decode_longctx.txt") if dist.world == 1 else None,
+                        "kernel": "decode_bulk_kernel", "kernel_ms": round(kms, 5),
+                        "algorithmic_bytes_per_launch": step_bytes},
+           # per step: decode_bulk_kernel; with several ranks also
+           # merge_lse_packed_kernel, with NCCL's all-gather between
+           "launches_per_step": 2 if dist.world > 1 else 1,
+           "clocks": clocks}
+    if dist.world == 1 and cpu_budget > 0:
+        v, thr, desc = cpu_decode_sample("longctx", cpu_budget)
+        res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port", "sample": desc}
+    return res
+
+
+def run_longctx(args, dist, peaks, res):
+    obj = run_longctx_obj(dist.device, args.steps, args.warmup, dist, peaks, 0 if args.no_cpu else args.cpu_budget)
+    res.update(obj)
+    res["metric"] = DECODE_METRIC
+    res["dtype"] = "f32 (bf16 KV)"
+    res["gpu_launches"] = args.steps * obj.pop("launches_per_step")
     emit(res, dist)
 
 
@@ -1037,6 +1131,10 @@ def main():
     ap.add_argument("--prefill-n", type=int, default=4, help="prefill sequences (llama3_prefill)")
     ap.add_argument("--prefill-s", type=int, default=8192, help="prefill tokens per sequence")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="default line without its batched_tinyllama and longctx objects")
+    ap.add_argument("--sub-steps", type=int, default=500,
+                    help="timed steps of the batched_tinyllama and longctx objects (at least --steps)")
     ap.add_argument("--gguf-threads", type=int, default=8, help="host threads of bml_gguf_upload (gguf_load)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=10.0)

@@ -61,8 +61,8 @@ class bml_gguf_value(C.Structure):
                 ("i", C.c_int64), ("f", C.c_double), ("str", C.c_void_p)]
 
 
-# name -> (restype, argtypes); mirrors include/bml_attn.h, bml_weights.h and
-# bml_gguf.h one to one.
+# name -> (restype, argtypes); mirrors include/bml_attn.h, bml_weights.h,
+# bml_gguf.h and bml_diag.h one to one.
 _vp, _u32, _i32, _st, _sz = C.c_void_p, C.c_uint32, C.c_int32, C.c_int32, C.c_size_t
 GGUF_F32, GGUF_F16, GGUF_Q4_0, GGUF_Q8_0 = 0, 1, 2, 8  # include/bml_weights.h
 SIGNATURES = {
@@ -115,9 +115,16 @@ SIGNATURES = {
     "bml_gguf_meta_find": (_st, [_vp, C.c_char_p, C.POINTER(C.c_uint64)]),
     "bml_gguf_meta_value": (_st, [_vp, C.c_uint64, C.POINTER(C.c_uint64), _u32, C.POINTER(bml_gguf_value)]),
     "bml_gguf_upload": (_st, [_vp, C.POINTER(C.c_uint64), _u32, C.POINTER(_vp), _u32]),
-    "bml_diag_exp2": (_st, [_vp, _u32, C.c_int, _vp, _vp]),
     "bml_attn_workspace_check": (_st, [_vp, _sz, _vp]),
+    "bml_attn_noalloc_check": (_st, [_vp]),
+    # include/bml_diag.h (test-only)
+    "bml_diag_exp2": (_st, [_vp, _u32, _vp, _vp]),
+    "bml_diag_decode_batched": (_st, [C.POINTER(bml_seq_desc), _u32, _u32, _u32, _u32, C.c_int,
+                                      C.c_float, _vp, _vp, _vp, _sz, C.c_int, C.c_uint64, _u32, _vp]),
 }
+
+BML_DIAG_DECODE_DEFAULT, BML_DIAG_DECODE_CUDA_CORE = 0, 1  # include/bml_diag.h
+BML_DIAG_STALL = 1
 
 _lock = threading.Lock()
 _lib = None

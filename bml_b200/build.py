@@ -26,25 +26,45 @@ def sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
 
 
+BUILD_DIR = os.path.join(HERE, "_build")
+FLAGS = ["-std=c++17", "-O3", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden"]
+
+
+def headers() -> list[str]:
+    return glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(HERE, "..", "include", "*.h"))
+
+
 def needs_build() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    deps = sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(
-        os.path.join(HERE, "..", "include", "*.h"))
-    return any(os.path.getmtime(d) > t for d in deps)
+    return any(os.path.getmtime(d) > t for d in sources() + headers())
+
+
+def _object(src: str, newest_header: float, force: bool, verbose: bool) -> str:
+    obj = os.path.join(BUILD_DIR, os.path.basename(src)[:-3] + ".o")
+    if force or not os.path.exists(obj) or os.path.getmtime(obj) < max(os.path.getmtime(src), newest_header):
+        cmd = [nvcc_path(), *FLAGS, "-c", "-o", obj + ".tmp", src]
+        if verbose:
+            cmd.insert(1, "-Xptxas=-v")
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+        os.replace(obj + ".tmp", obj)
+    return obj
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compiles every csrc/*.cu to an object (in parallel, each only when it
+    or a header changed) and links libbmlattn.so."""
     if not force and not needs_build():
         return LIB
-    cmd = [nvcc_path(), "-std=c++17", "-O3", *ARCH, "-lineinfo",
-           "-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared",
-           "-o", LIB + ".tmp", *sources()]
-    if verbose:
-        cmd.insert(3, "-Xptxas=-v")
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True)
+    from concurrent.futures import ThreadPoolExecutor
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    newest = max((os.path.getmtime(h) for h in headers()), default=0.0)
+    srcs = sources()
+    with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
+        objs = list(ex.map(lambda f: _object(f, newest, force, verbose), srcs))
+    subprocess.run([nvcc_path(), *ARCH, "-shared", "-o", LIB + ".tmp", *objs], check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

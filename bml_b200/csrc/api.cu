@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "../../include/bml_attn.h"
+#include "../../include/bml_diag.h"
 #include "../../include/bml_weights.h"
 #include "decode.cuh"
 #include "gemv.cuh"
@@ -424,17 +425,74 @@ bml_status check_decode_shape(uint32_t n_heads, uint32_t n_kv, uint32_t head_dim
     return BML_OK;
 }
 
-// Shared body of bml_attn_decode_batched / _partial.
+// Schedule knobs of the claimed-schedule kernel (decode_bulk_kernel).
+struct BulkPlan {
+    uint32_t claim_tiles = 2;  // tiles per claim
+    uint32_t join_min = 8;     // unclaimed tiles worth a join
+    uint32_t merge_rows = 8;   // q-head rows per merge item
+    uint32_t merge_wpr = 1;    // warps sharing one row in the merge
+    uint32_t merge_dsplit = 1; // head-dim slices per merge item
+};
+
+// Tiles per claim: two (~2.6 us of one SM at the HBM rate; measured on
+// B200: with one tile a claim's atomic, issued one claim ahead, no longer
+// hides behind the ring and the Llama-3 batch streams at 6.0 instead of 7.3
+// TB/s).  A started sequence is joined only while it has at least 4 claims
+// left: a join costs three dependent round trips (~3 us).
+// Merge: a row of a sequence has about nph * (grid / n_seqs + 2) partial
+// slots; each warp combines up to 16 of them in one round of loads, so a
+// row is shared by up to 8 warps (one long sequence: one row per CTA), and
+// where one warp per row suffices and the items would not fit one round of
+// the grid, a warp takes two rows.  join_min: a started sequence is joined
+// only while it has at least 4 claims left.
+BulkPlan bulk_plan(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, uint32_t nph, uint32_t parts_per_seq,
+                   int grid) {
+    BulkPlan b;
+    const uint32_t per_row = std::min<uint32_t>(parts_per_seq, (uint32_t)grid / n_seqs + 2u) * nph;
+    uint32_t wpr = 1;
+    while (wpr < 8 && per_row > 16u * wpr) wpr *= 2;
+    uint32_t rows = 8u / wpr;
+    if (wpr == 1 && n_heads % 16u == 0 && (uint64_t)n_seqs * n_heads / 8u > (uint64_t)grid) rows = 16;
+    while (rows > 1 && n_heads % rows) rows /= 2;  // small head counts
+    if (rows * wpr < 8u) wpr = 8u / rows;
+    b.merge_rows = rows;
+    b.merge_wpr = wpr;
+    // few rows with many slots each (a long sequence): split the head dims
+    // too, so that more CTAs share the merge and each lane keeps all its
+    // slots in flight at once
+    while (b.merge_dsplit < 4 && wpr == 8 && 32u * b.merge_dsplit * 2u <= head_dim &&
+           (uint64_t)n_seqs * (n_heads / rows) * b.merge_dsplit * 2u <= (uint64_t)grid)
+        b.merge_dsplit *= 2;
+    return b;
+}
+
+// Home CTAs of the busiest sequence of a claimed-schedule launch (each takes
+// one part of it statically).
+uint32_t max_homes(const bml::DecodeParams &p, uint32_t total, uint32_t grid) {
+    uint32_t m = 0;
+    for (uint32_t s = 0; s < p.n_seqs; ++s) {
+        const uint32_t lo = bml::decode_home_lo(p.seqs[s].tile_begin, total, grid);
+        const uint32_t hi = s + 1 < p.n_seqs ? bml::decode_home_lo(p.seqs[s + 1].tile_begin, total, grid) : grid;
+        m = std::max(m, hi - lo);
+    }
+    return m;
+}
+
+// Shared body of bml_attn_decode_batched / _partial (and their test-only
+// variant, whose kernel choice, wait limit and behaviour flags are given).
 bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv,
                        uint32_t head_dim, bml_dtype dt, float scale, const float *q, float *out, float *pm,
                        float *pl, float *po, void *workspace, size_t ws_bytes, void *stream, int mode,
-                       const char *fn) {
+                       const char *fn, int force_kernel = 0, uint64_t wait_ns = bml::kWaitNs, uint32_t diag = 0) {
     bml_status st = check_decode_shape(n_heads, n_kv, head_dim, dt, fn);
     if (st != BML_OK) return st;
     if (!seqs || n_seqs == 0) return fail(BML_E_INVALID, "%s: no sequences", fn);
     if (!q || !aligned16(q)) return fail(BML_E_INVALID, "%s: q must be a 16-byte aligned device pointer", fn);
-    if (mode == bml::kModeFinal && !out) return fail(BML_E_INVALID, "%s: null output", fn);
-    if (mode == bml::kModePartial && (!pm || !pl || !po)) return fail(BML_E_INVALID, "%s: null output", fn);
+    if (mode == bml::kModeFinal && (!out || !aligned16(out)))
+        return fail(BML_E_INVALID, "%s: out must be a 16-byte aligned device pointer", fn);
+    if (mode == bml::kModePartial && (!pm || !pl || !po || !aligned16(po)))
+        return fail(BML_E_INVALID, "%s: null or misaligned partial output", fn);
+    if (!aligned16(workspace)) return fail(BML_E_INVALID, "%s: workspace must be 16-byte aligned", fn);
     for (uint32_t s = 0; s < n_seqs; ++s) {
         if (seqs[s].len == 0) return fail(BML_E_INVALID, "%s: sequence %u has no positions", fn, s);
         if (!seqs[s].k_dev || !seqs[s].v_dev || !aligned16(seqs[s].k_dev) || !aligned16(seqs[s].v_dev))
@@ -443,95 +501,75 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
     const int dev = current_device();
     const int sms = num_sms(dev);
     bml::DecodeWorkspace ws;
-    if (!bml::decode_workspace_carve(workspace, ws_bytes, n_seqs, n_heads, head_dim, sms, &ws))
+    if (!bml::decode_workspace_carve(workspace, ws_bytes, n_seqs, n_heads, n_kv, head_dim, sms, &ws))
         return fail(BML_E_INVALID, "%s: workspace of %zu bytes, need %zu", fn, ws_bytes,
-                    bml::decode_workspace_min_bytes(n_seqs, n_heads, head_dim, sms));
+                    bml::decode_workspace_min_bytes(n_seqs, n_heads, n_kv, head_dim, sms));
 
     const float sc = resolve_scale(scale, head_dim);
     const size_t es = bml::dtype_size(dt);
     const uint32_t T = bml::decode_rows_per_tile(dt, head_dim, n_kv);
     const uint32_t group = n_heads / n_kv;
+    const bml::DecodeKernel kern =
+        force_kernel == BML_DIAG_DECODE_CUDA_CORE ? bml::kKernCuda : bml::decode_select(dt, head_dim, n_kv, group);
     static thread_local bml::DecodeParams p;  // ~8 KB, kept off the stack
-    // the TMA kernel carries two tensor maps per sequence in its parameters:
-    // when it is forced, launches take at most its 64 sequences
-    const uint32_t chunk = bml::decode_family_override() == bml::kDecodeTma &&
-                                   bml::decode_tma_supported(dt, head_dim, n_kv, group)
-                               ? bml::decode_tma_max_seqs()
-                               : (uint32_t)bml::kMaxSeqsPerLaunch;
-    for (uint32_t base = 0; base < n_seqs; base += chunk) {
-        const uint32_t ns = std::min<uint32_t>(n_seqs - base, chunk);
+    for (uint32_t base = 0; base < n_seqs; base += (uint32_t)bml::kMaxSeqsPerLaunch) {
+        const uint32_t ns = std::min<uint32_t>(n_seqs - base, (uint32_t)bml::kMaxSeqsPerLaunch);
         memset(&p, 0, offsetof(bml::DecodeParams, seqs));
         p.n_seqs = ns;
         p.n_kv = n_kv;
         uint64_t total = 0;
+        uint32_t slot = 0, max_slots_seq = 0;
         for (uint32_t s = 0; s < ns; ++s) {
             const bml_seq_desc &d = seqs[base + s];
             bml::DecodeSeq &e = p.seqs[s];
             e.k = d.k_dev;
             e.v = d.v_dev;
             e.len = d.len;
+            e.tile_begin = (uint32_t)total;
             total += (d.len + T - 1) / T;
         }
-        if (total > 0xffffffffull) return fail(BML_E_INVALID, "%s: batch too large", fn);
-        const bml::DecodeKernel kern = bml::decode_select(p, dt, head_dim, group);
+        if (total > 0x7fffffffull) return fail(BML_E_INVALID, "%s: batch too large", fn);
         int grid = 0;
-        uint32_t slot = 0, max_slots_seq = 0;
         if (kern == bml::kKernBulk) {
-            // Dynamic schedule: chunks of C tiles, about 6 per SM, claimed at
-            // run time (measured: 4-12 per SM within 3% on batches; fewer
-            // is better for one long sequence, where the partials' traffic
-            // and merge weigh more), and at least 8 tiles (measured on a
-            // small batch, 147 MB of KV: a minimum of 8 tiles beats 4, whose
-            // extra slots cost more in the merge than the finer split gains,
-            // and 12 or 16, which leave too few chunks to balance; likewise
-            // on the 32-request serving loop).  Each chunk leaves one partial slot per
-            // warp of a kv head (8 / n_kv), so C grows until the slots fit
-            // the workspace and a sequence has at most 512 of them.
-            const uint32_t nph = 8u / n_kv;
-            uint64_t C = std::max<uint64_t>(8, (total + 6ull * sms - 1) / (6ull * sms));
-            auto fits = [&](uint64_t c) {
-                uint64_t n = 0;
-                for (uint32_t s = 0; s < ns; ++s) {
-                    const uint64_t k = ((p.seqs[s].len + T - 1) / T + c - 1) / c;
-                    if (k * nph > 512) return false;
-                    n += k;
-                }
-                return n * nph <= ws.max_slots;
-            };
-            while (!fits(C)) C = C + C / 4 + 1;
-            uint32_t chunk_no = 0;
-            for (uint32_t s = 0; s < ns; ++s) {
-                bml::DecodeSeq &e = p.seqs[s];
-                const uint32_t nc = (uint32_t)(((e.len + T - 1) / T + C - 1) / C);
-                e.tile_begin = chunk_no;
-                e.slot_base = chunk_no * nph;
-                e.n_slots = nc * nph;
-                chunk_no += nc;
-                max_slots_seq = std::max(max_slots_seq, e.n_slots);
+            // Claimed schedule: at most one CTA per SM and per tile; parts
+            // per sequence as the workspace's slots allow (each CTA visits a
+            // sequence at most once, so more than `grid` are never used) and
+            // at least the busiest sequence's home CTAs (fewer CTAs if the
+            // slots are short).
+            grid = (int)std::min<uint64_t>((uint64_t)sms, total);
+            const uint32_t nph = bml::decode_bulk_phases(n_kv);
+            size_t pps = 0;
+            while (true) {
+                pps = std::min<size_t>({(size_t)grid, ws.max_slots / ((size_t)ns * nph), bml::kMaxPartTiles / ns});
+                if (pps >= std::max<uint32_t>(1u, max_homes(p, (uint32_t)total, (uint32_t)grid)) || grid == 1) break;
+                grid = std::max(1, grid * 3 / 4);
             }
-            slot = chunk_no * nph;
-            p.chunk_tiles = (uint32_t)C;
-            p.total_chunks = chunk_no;
+            if (pps == 0) return fail(BML_E_INVALID, "%s: internal part overflow", fn);
+            const BulkPlan plan = bulk_plan(ns, n_heads, head_dim, nph, (uint32_t)pps, grid);
+            p.parts_per_seq = (uint32_t)pps;
+            p.claim_tiles = plan.claim_tiles;
+            p.join_min = plan.join_min;
+            p.merge_rows = plan.merge_rows;
+            p.merge_wpr = plan.merge_wpr;
+            p.merge_dsplit = plan.merge_dsplit;
             p.sched = ws.sched;
-            grid = (int)std::min<uint32_t>((uint32_t)sms, chunk_no);
+            p.part_tiles = ws.part_tiles;
         } else {
             // Static schedule: contiguous ranges of tpc tiles per CTA.
             const uint32_t tpc = (uint32_t)((total + sms - 1) / sms);
             grid = (int)((total + tpc - 1) / tpc);
-            uint32_t tile = 0;
             for (uint32_t s = 0; s < ns; ++s) {
                 bml::DecodeSeq &e = p.seqs[s];
                 const uint32_t nt = (e.len + T - 1) / T;
-                e.tile_begin = tile;
                 e.slot_base = slot;
-                e.n_slots = (tile + nt - 1) / tpc - tile / tpc + 1;
-                tile += nt;
+                e.n_slots = (e.tile_begin + nt - 1) / tpc - e.tile_begin / tpc + 1;
                 slot += e.n_slots;
                 max_slots_seq = std::max(max_slots_seq, e.n_slots);
             }
+            if (slot > ws.max_slots) return fail(BML_E_INVALID, "%s: internal slot overflow", fn);
             p.tiles_per_cta = tpc;
+            p.merge_in_kernel = max_slots_seq <= bml::kInKernelMergeMaxSlots ? 1 : 0;
         }
-        if (slot > ws.max_slots) return fail(BML_E_INVALID, "%s: internal slot overflow", fn);
         p.q = q + (size_t)base * n_heads * head_dim;
         p.out = out ? out + (size_t)base * n_heads * head_dim : nullptr;
         p.part_m = pm ? pm + (size_t)base * n_heads : nullptr;
@@ -547,12 +585,15 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
         p.row_bytes = (uint32_t)(n_kv * head_dim * es);
         p.qscale = (float)((double)sc * 1.4426950408889634);
         p.mode = mode;
-        // the bulk kernel leaves every multi-slot sequence to launch_slot_merge
-        p.merge_in_kernel = kern == bml::kKernBulk ? (max_slots_seq <= 1 ? 1 : 0)
-                                                   : (max_slots_seq <= bml::kInKernelMergeMaxSlots ? 1 : 0);
-        CUDA_TRY(bml::launch_decode(p, kern, dt, head_dim, group, grid, static_cast<cudaStream_t>(stream)), fn);
-        if (!p.merge_in_kernel)
-            CUDA_TRY(bml::launch_slot_merge(p, head_dim, static_cast<cudaStream_t>(stream)), fn);
+        p.wait_ns = wait_ns;
+        p.diag = diag;
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (kern == bml::kKernBulk) {
+            CUDA_TRY(bml::launch_decode_bulk(p, dt, head_dim, group, grid, s), fn);
+        } else {
+            CUDA_TRY(bml::launch_decode(p, dt, head_dim, group, grid, s), fn);
+            if (!p.merge_in_kernel) CUDA_TRY(bml::launch_slot_merge(p, head_dim, s), fn);
+        }
     }
     return ok();
 }
@@ -749,12 +790,28 @@ BML_API bml_status bml_attn_prefill(const void *q_dev, const void *k_dev, const 
     return ok();
 }
 
-BML_API bml_status bml_diag_exp2(const float *x_dev, uint32_t n, int method, float *out_dev, void *stream) {
-    if (!x_dev || !out_dev || (n & 1u) || (method != 0 && method != 1))
-        return fail(BML_E_INVALID, "bml_diag_exp2: bad argument");
+// ---------------------------------------------------------------------------
+// Test-only entry points (include/bml_diag.h)
+// ---------------------------------------------------------------------------
+BML_API bml_status bml_diag_exp2(const float *x_dev, uint32_t n, float *out_dev, void *stream) {
+    if (!x_dev || !out_dev || (n & 1u)) return fail(BML_E_INVALID, "bml_diag_exp2: bad argument");
     if (!aligned16(x_dev) || !aligned16(out_dev)) return fail(BML_E_INVALID, "bml_diag_exp2: alignment");
-    CUDA_TRY(bml::diag_exp2(x_dev, n, method, out_dev, static_cast<cudaStream_t>(stream)), "bml_diag_exp2");
+    CUDA_TRY(bml::diag_exp2(x_dev, n, out_dev, static_cast<cudaStream_t>(stream)), "bml_diag_exp2");
     return ok();
+}
+
+BML_API bml_status bml_diag_decode_batched(const bml_seq_desc *seqs_host, uint32_t n_seqs, uint32_t n_heads,
+                                           uint32_t n_kv_heads, uint32_t head_dim, bml_dtype kv_dtype, float scale,
+                                           const float *q_dev, float *out_dev, void *workspace,
+                                           size_t workspace_bytes, int kernel, uint64_t wait_ns, uint32_t flags,
+                                           void *stream) {
+    const char *fn = "bml_diag_decode_batched";
+    if (kernel != BML_DIAG_DECODE_DEFAULT && kernel != BML_DIAG_DECODE_CUDA_CORE)
+        return fail(BML_E_INVALID, "%s: kernel %d", fn, kernel);
+    if (flags & ~BML_DIAG_STALL) return fail(BML_E_INVALID, "%s: flags 0x%x", fn, flags);
+    return decode_impl(seqs_host, n_seqs, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev, nullptr,
+                       nullptr, nullptr, workspace, workspace_bytes, stream, bml::kModeFinal, fn, kernel,
+                       wait_ns ? wait_ns : bml::kWaitNs, (flags & BML_DIAG_STALL) ? bml::kDiagStall : 0u);
 }
 
 // ---------------------------------------------------------------------------
@@ -816,7 +873,7 @@ BML_API bml_status bml_attn_decode_batched_noalloc(const bml_seq_desc *seqs_host
     if (st != BML_OK) return st;
     if (!seqs_host || n_seqs == 0) return fail(BML_E_INVALID, "%s: no sequences", fn);
     const int dev = current_device();
-    const size_t need = bml::decode_workspace_min_bytes(n_seqs, n_heads, head_dim, num_sms(dev));
+    const size_t need = bml::decode_workspace_min_bytes(n_seqs, n_heads, n_kv_heads, head_dim, num_sms(dev));
     if (need > kNoAllocScratchBytes)
         return fail(BML_E_INVALID, "%s: needs %zu bytes of scratch, above the fixed %zu-byte maximum", fn, need,
                     kNoAllocScratchBytes);
@@ -824,11 +881,21 @@ BML_API bml_status bml_attn_decode_batched_noalloc(const bml_seq_desc *seqs_host
     st = noalloc_scratch(dev, &scratch);
     if (st != BML_OK) return st;
     // Every call shares the array, which keeps the last call's contents:
-    // clear the error word and the merge tickets, which must start at zero.
-    CUDA_TRY(cudaMemsetAsync(scratch, 0, bml::decode_workspace_zero_bytes(), static_cast<cudaStream_t>(stream)),
+    // clear the schedule counters, which must start at zero (each call also
+    // leaves them zero).  The error word at offset 0 is left alone, so that
+    // a timeout stays recorded until bml_attn_noalloc_check reads it.
+    CUDA_TRY(cudaMemsetAsync(static_cast<uint8_t *>(scratch) + 64, 0, bml::decode_workspace_zero_bytes() - 64,
+                             static_cast<cudaStream_t>(stream)),
              fn);
     return decode_impl(seqs_host, n_seqs, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev, nullptr,
                        nullptr, nullptr, scratch, kNoAllocScratchBytes, stream, bml::kModeFinal, fn);
+}
+
+BML_API bml_status bml_attn_noalloc_check(void *stream) {
+    void *scratch = nullptr;
+    bml_status st = noalloc_scratch(current_device(), &scratch);
+    if (st != BML_OK) return st;
+    return bml_attn_workspace_check(scratch, kNoAllocScratchBytes, stream);
 }
 
 // ---------------------------------------------------------------------------

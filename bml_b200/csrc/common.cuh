@@ -12,10 +12,11 @@
 namespace bml {
 
 // ---------------------------------------------------------------------------
-// Bounded waits.  Every spin on an mbarrier gives up after kWaitNs
-// nanoseconds of %globaltimer, records BML_E_TIMEOUT in the kernel's error
-// word and lets the CTA run to its end without waiting again, so that no
-// kernel of this library can hang a GPU.
+// Bounded waits.  Every spin on an mbarrier or a global counter gives up
+// after kWaitNs nanoseconds of %globaltimer (or a limit passed at launch),
+// records BML_E_TIMEOUT in the kernel's error word and lets the CTA run to
+// its end without waiting again, so that no kernel of this library can hang
+// a GPU.
 // ---------------------------------------------------------------------------
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
 constexpr uint32_t kErrTimeout = 1u;
@@ -81,21 +82,48 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
 
 // Waits for phase `parity` of `bar` to complete.  `abort_flag` (shared) is
 // set once any wait of the CTA timed out; later waits then return at once.
-// Returns false on timeout.
+// Returns false on timeout.  `limit_ns` bounds the wait (kWaitNs unless a
+// kernel takes its limit as a launch parameter).
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          volatile uint32_t *abort_flag, uint32_t *err) {
+                                          volatile uint32_t *abort_flag, uint32_t *err,
+                                          uint64_t limit_ns = kWaitNs) {
     if (mbar_test_wait(bar, parity)) return true;
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer_ns();
     while (true) {
         if (*abort_flag) return false;
         if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer_ns() - t0 > kWaitNs) {
+        if (globaltimer_ns() - t0 > limit_ns) {
             *abort_flag = 1u;
             if (err) atomicOr(err, kErrTimeout);
             return false;
         }
     }
+}
+
+// Waits (bounded by limit_ns, ignoring any abort flag) for phase `parity`
+// of `bar`: used before a CTA leaves, so that no bulk copy it issued is
+// still writing its shared memory.
+__device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity, uint64_t limit_ns) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+    return true;
+}
+
+// Global-memory loads for counters that other CTAs update: acquire (orders
+// the caller's later reads after the value) and relaxed (a fresh value from
+// L2, no ordering).
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // 1-D bulk copy global -> shared, completing on an mbarrier (TMA unit).
@@ -141,31 +169,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
     float r;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-    return r;
-}
-
-// 2^x for a pair of values on the FMA and ALU pipes instead of the SFU,
-// for x in [-126, 126] (smaller x is clamped to 2^-126).  Method: Cody-Waite
-// range reduction x = j + f with j = round(x), f in [-0.5, 0.5] (the
-// rounding is done by adding 1.5*2^23, which also leaves j in the low
-// mantissa bits), then 2^f by a cubic with c0 = 1 whose other coefficients
-// were least-squares fitted for this library on Chebyshev nodes (max
-// relative error 1.0e-4 on [-0.5, 0.5]), and 2^j applied by adding j to
-// the exponent field.  Used for part of the softmax exponentials whose
-// results are rounded to 16 bits, where 1e-4 is far below the rounding.
-__device__ __forceinline__ float2 exp2_poly2(float2 x) {
-    const float2 magic = make_float2(12582912.0f, 12582912.0f);
-    x.x = fmaxf(x.x, -126.0f);
-    x.y = fmaxf(x.y, -126.0f);
-    const float2 t = __fadd2_rn(x, magic);
-    const float2 jf = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
-    const float2 f = __ffma2_rn(jf, make_float2(-1.0f, -1.0f), x);
-    float2 p = __ffma2_rn(make_float2(0.05500892f, 0.05500892f), f, make_float2(0.24221097f, 0.24221097f));
-    p = __ffma2_rn(p, f, make_float2(0.69328290f, 0.69328290f));
-    p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
-    float2 r;
-    r.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
-    r.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
     return r;
 }
 

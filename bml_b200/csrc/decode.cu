@@ -33,6 +33,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
+
 #include "decode.cuh"
 
 namespace bml {
@@ -224,7 +226,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_kernel(const __grid_constan
 
     for (uint32_t t = t_begin, it = 0; t < t_end; ++t, ++it) {
         const uint32_t stage = it % NST;
-        mbar_wait(&full[stage], (it / NST) & 1u, flags, p.err);
+        mbar_wait(&full[stage], (it / NST) & 1u, flags, p.err, p.wait_ns);
         __syncwarp();  // lanes leave the spin separately; the shuffles below need the whole warp
         const uint32_t row0 = (t - p.seqs[s].tile_begin) * T;
         const uint32_t rows = min(T, p.seqs[s].len - row0);
@@ -703,23 +705,31 @@ uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv) {
 }
 
 // Scratch layout, fixed part first so that calls of any shape agree on it:
-//   [0, 64)                   error word
-//   [64, 72)                  dynamic-schedule claim counter and CTA exit
-//                             ticket; each call leaves them zero
-//   [256, 256 + kTicketBytes) merge tickets: one per (sequence, kv head) of a
-//                             launch (256 sequences x 8 kv heads at most); each
-//                             call leaves them zero
+//   [0, 64)                   error word (kept until read by a check call)
+//   [64, 256)                 claimed-schedule words: CTA exit ticket, merge-
+//                             item claims; each call leaves them zero
+//   [256, 256 + kTicketBytes) per-sequence counters of a launch (256
+//                             sequences at most): tile claims, part
+//                             reservations, tiles done (claimed schedule) or
+//                             merge tickets (static schedule); each call
+//                             leaves them zero
+//   [.., + kPartTileBytes)    tiles in each part of the claimed schedule
+//                             (kMaxPartTiles words); each call leaves them zero
 //   then partial slots of n_heads rows each: as many as the workspace holds,
-//   at least 2*seqs + SMs (the static schedule's split points); the
-//   recommended size holds 2*seqs + 8*SMs (dynamic-schedule chunks).
-// A shape-dependent ticket area would let one call read another call's
-// leftover slot values as tickets.
+//   at least 2*seqs + SMs (the static schedule's split points) and one part
+//   of every sequence (claimed schedule); the recommended size holds 2*seqs
+//   + 8*SMs.
+// A shape-dependent counter area would let one call read another call's
+// leftover slot values as counters.
 constexpr size_t kTicketBytes = (size_t)kMaxSeqsPerLaunch * 8 * 4;
+constexpr size_t kPartTileBytes = kMaxPartTiles * 4;
 
 namespace {
 
+constexpr size_t kFixedBytes = 256 + kTicketBytes + kPartTileBytes;
+
 size_t workspace_bytes_for(size_t slots, uint32_t n_heads, uint32_t head_dim) {
-    size_t b = 256 + kTicketBytes;
+    size_t b = kFixedBytes;
     b += ((slots * n_heads * 2 * 4 + 255) / 256) * 256;   // slot (m, l)
     b += slots * n_heads * head_dim * 4;                  // slot o
     return b;
@@ -730,21 +740,29 @@ size_t launch_seqs(uint32_t n_seqs) { return n_seqs < (uint32_t)kMaxSeqsPerLaunc
 }  // namespace
 
 size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, int num_sms) {
-    return workspace_bytes_for(2 * launch_seqs(n_seqs) + 8 * (size_t)num_sms, n_heads, head_dim);
+    return workspace_bytes_for(std::max<size_t>(2 * launch_seqs(n_seqs) + 8 * (size_t)num_sms,
+                                                8 * launch_seqs(n_seqs)),
+                               n_heads, head_dim);
 }
 
-size_t decode_workspace_min_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, int num_sms) {
-    return workspace_bytes_for(2 * launch_seqs(n_seqs) + (size_t)num_sms, n_heads, head_dim);
+size_t decode_workspace_min_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv, uint32_t head_dim,
+                                  int num_sms) {
+    // the static schedule's split points, and one part of every sequence of
+    // a claimed-schedule launch (8 / n_kv slots a part)
+    const size_t nph = n_kv && n_kv <= 8 ? 8 / n_kv : 8;
+    return workspace_bytes_for(std::max<size_t>(2 * launch_seqs(n_seqs) + (size_t)num_sms,
+                                                nph * launch_seqs(n_seqs)),
+                               n_heads, head_dim);
 }
 
-size_t decode_workspace_zero_bytes() { return 256 + kTicketBytes; }
+size_t decode_workspace_zero_bytes() { return kFixedBytes; }
 
-bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
-                            int num_sms, DecodeWorkspace *out) {
-    if (!ws || bytes < decode_workspace_min_bytes(n_seqs, n_heads, head_dim, num_sms)) return false;
+bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv,
+                            uint32_t head_dim, int num_sms, DecodeWorkspace *out) {
+    if (!ws || bytes < decode_workspace_min_bytes(n_seqs, n_heads, n_kv, head_dim, num_sms)) return false;
     // the largest slot count whose layout fits in `bytes`
     const size_t per_slot = (size_t)n_heads * (2 + head_dim) * 4;
-    size_t slots = (bytes - 256 - kTicketBytes - 256) / per_slot;
+    size_t slots = (bytes - kFixedBytes - 256) / per_slot;
     while (slots > 0 && workspace_bytes_for(slots, n_heads, head_dim) > bytes) --slots;
     uint8_t *b = static_cast<uint8_t *>(ws);
     out->err = reinterpret_cast<uint32_t *>(b);
@@ -752,6 +770,8 @@ bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_
     b += 256;
     out->counters = reinterpret_cast<uint32_t *>(b);
     b += kTicketBytes;
+    out->part_tiles = reinterpret_cast<uint32_t *>(b);
+    b += kPartTileBytes;
     out->slot_ml = reinterpret_cast<float *>(b);
     b += ((slots * n_heads * 2 * 4 + 255) / 256) * 256;
     out->slot_o = reinterpret_cast<float *>(b);
@@ -759,41 +779,12 @@ bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_
     return true;
 }
 
-DecodeFamily decode_family_override() {
-    static const DecodeFamily fam = [] {
-        const char *v = getenv("BML_DECODE_KERNEL");
-        if (v && strcmp(v, "mma") == 0) return kDecodeMma;
-        if (v && strcmp(v, "cuda") == 0) return kDecodeCuda;
-        if (v && strcmp(v, "bulk") == 0) return kDecodeBulk;
-        if (v && strcmp(v, "tma") == 0) return kDecodeTma;
-        return kDecodeAuto;
-    }();
-    return fam;
+DecodeKernel decode_select(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group) {
+    return decode_bulk_supported(dt, head_dim, n_kv, group) ? kKernBulk : kKernCuda;
 }
 
-DecodeKernel decode_select(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group) {
-    // 16-bit caches of the common shapes take the tensor-core kernels: group
-    // bulk copies with the dynamic schedule (decode_bulk.cu) by default, TMA
-    // tile loads (decode_tma.cu) or cp.async loads (decode_mma.cu) where it
-    // does not apply or is overridden; everything else the CUDA-core kernel.
-    const DecodeFamily fam = decode_family_override();
-    const bool tma_ok = p.n_seqs <= decode_tma_max_seqs() && decode_tma_supported(dt, head_dim, p.n_kv, group);
-    const bool bulk_ok = decode_bulk_supported(dt, head_dim, p.n_kv, group);
-    if (fam == kDecodeTma && tma_ok) return kKernTma;
-    if ((fam == kDecodeBulk || fam == kDecodeAuto) && bulk_ok) return kKernBulk;
-    if (fam == kDecodeAuto && tma_ok) return kKernTma;
-    if (fam != kDecodeCuda && decode_mma_supported(dt, head_dim, p.n_kv, group)) return kKernMma;
-    return kKernCuda;
-}
-
-cudaError_t launch_decode(const DecodeParams &p, DecodeKernel kern, bml_dtype dt, uint32_t head_dim,
-                          uint32_t group, int grid, cudaStream_t stream) {
-    switch (kern) {
-        case kKernTma: return launch_decode_tma(p, dt, head_dim, group, grid, stream);
-        case kKernBulk: return launch_decode_bulk(p, dt, head_dim, group, grid, stream);
-        case kKernMma: return launch_decode_mma(p, dt, head_dim, group, grid, stream);
-        case kKernCuda: break;
-    }
+cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group, int grid,
+                          cudaStream_t stream) {
     switch (dt) {
         case BML_F32: return launch_d<float>(p, head_dim, group, grid, stream);
         case BML_F16: return launch_d<__half>(p, head_dim, group, grid, stream);

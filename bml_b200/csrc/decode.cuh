@@ -6,25 +6,28 @@
 namespace bml {
 
 // Per-sequence entry of a decode launch (host-computed schedule).
-// Static schedule (chunk_tiles == 0): CTA b owns global tiles
+// Static schedule (decode_kernel): CTA b owns global tiles
 // [b*tiles_per_cta, (b+1)*tiles_per_cta); tile_begin is the sequence's first
 // global tile and its n_slots partial slots are one per CTA touching it.
-// Dynamic schedule (chunk_tiles > 0): the sequence is cut into n_slots
-// chunks of chunk_tiles tiles, global chunk indices [tile_begin, tile_begin
-// + n_slots); CTAs claim chunks at run time and chunk c leaves its partial
-// in slot c (slot_base == tile_begin).
+// Claimed schedule (decode_bulk_kernel): tile_begin is the sequence's first
+// global tile (prefix of the tile counts); CTAs claim the sequence's tiles
+// at run time and leave at most parts_per_seq parts of it.
 struct DecodeSeq {
     const void *k;        // [len][n_kv][D]
     const void *v;
     uint32_t len;         // positions attended
-    uint32_t tile_begin;  // first global tile (static) or chunk (dynamic)
-    uint32_t slot_base;   // first partial slot of this sequence
-    uint32_t n_slots;     // CTAs (static) or chunks (dynamic) of this sequence
+    uint32_t tile_begin;  // first global tile of this sequence
+    uint32_t slot_base;   // static schedule: first partial slot of this sequence
+    uint32_t n_slots;     // static schedule: CTAs touching this sequence
 };
 
 constexpr int kMaxSeqsPerLaunch = 256;
 
 enum DecodeMode : int { kModeFinal = 0, kModePartial = 1 };
+
+// Test-only behaviour of decode_bulk_kernel (bml_diag_decode_batched): the
+// producer arms no stage, so every consumer wait runs into its limit.
+constexpr uint32_t kDiagStall = 1u;
 
 struct DecodeParams {
     const float *q;        // [n_seqs][n_heads][D] f32
@@ -34,21 +37,29 @@ struct DecodeParams {
     float *part_o;         // [n_seqs][n_heads][D]
     float *slot_ml;        // scratch [n_slots][n_heads][2]
     float *slot_o;         // scratch [n_slots][n_heads][D]
-    uint32_t *counters;    // scratch [n_seqs], zero between calls
+    uint32_t *counters;    // scratch [4][kMaxSeqsPerLaunch] words, zero between calls
     uint32_t *err;         // scratch error word
     uint32_t n_seqs, n_heads, n_kv;
     uint32_t rows_per_tile;   // T
     uint32_t total_tiles;
-    uint32_t tiles_per_cta;
+    uint32_t tiles_per_cta;   // static schedule
     uint32_t row_bytes;       // n_kv * D * sizeof(elem)
     float qscale;             // scale * log2(e)
     int mode;
-    int merge_in_kernel;      // 1: last CTA of a sequence merges its slots;
-                              // 0: slots are merged by launch_slot_merge
-    uint32_t chunk_tiles;     // dynamic schedule: tiles per chunk (0: static)
-    uint32_t total_chunks;
-    uint32_t *sched;          // dynamic schedule: [0] chunk claims, [1] CTA exit
-                              // ticket; zero between calls
+    int merge_in_kernel;      // static schedule: 1 = the last CTA of a sequence
+                              // merges its slots, 0 = launch_slot_merge does
+    // claimed schedule (decode_bulk_kernel)
+    uint32_t *sched;          // [0] CTA exit ticket, [1] merge items claimed, [2] sequences
+                              // completed; zero between calls
+    uint32_t *part_tiles;     // [n_seqs * parts_per_seq] tiles in each part (0: empty); zero between calls
+    uint32_t parts_per_seq;   // parts a sequence may have (>= 1)
+    uint32_t claim_tiles;     // tiles per claim
+    uint32_t join_min;        // unclaimed tiles that make a started sequence worth joining
+    uint32_t merge_rows;      // q-head rows per merge item (1, 2, 4, 8 or 16)
+    uint32_t merge_wpr;       // consumer warps sharing one row in the merge (1, 2, 4 or 8)
+    uint32_t merge_dsplit;    // head-dim slices of a row block, one merge item each (1, 2 or 4)
+    uint32_t diag;            // kDiag* flags, 0 outside tests
+    uint64_t wait_ns;         // limit of every bounded wait
     DecodeSeq seqs[kMaxSeqsPerLaunch];
 };
 
@@ -57,68 +68,64 @@ struct DecodeWorkspace {
     uint32_t *err;
     uint32_t *sched;
     uint32_t *counters;
+    uint32_t *part_tiles;
     float *slot_ml;
     float *slot_o;
     size_t max_slots;
 };
 
-// Recommended scratch bytes (room for the dynamic schedule's chunk slots)
-// and the minimum a call accepts (the static schedule's slots); the
-// dynamic schedule sizes its chunks to the slots a workspace holds.
+// Recommended scratch bytes and the minimum a call accepts.  A slot holds
+// one partial (m, l, o) for every q head of a sequence.
 size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
                               int num_sms);
-size_t decode_workspace_min_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim,
+size_t decode_workspace_min_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv, uint32_t head_dim,
                                   int num_sms);
-// Bytes at the start of a workspace that must be zero before a call
-// (error word and merge tickets).
+// Bytes at the start of a workspace that must be zero before a call (error
+// word, schedule counters, part tile counts); every call leaves all but the
+// error word zero, and the error word keeps a timeout until it is checked.
 size_t decode_workspace_zero_bytes();
-bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads,
+bool decode_workspace_carve(void *ws, size_t bytes, uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv,
                             uint32_t head_dim, int num_sms, DecodeWorkspace *out);
 
 // Rows of one tile for a (dtype, head_dim, n_kv) combination.
 uint32_t decode_rows_per_tile(bml_dtype dt, uint32_t head_dim, uint32_t n_kv);
 
-enum DecodeKernel : int { kKernTma = 0, kKernBulk = 1, kKernMma = 2, kKernCuda = 3 };
+enum DecodeKernel : int { kKernBulk = 1, kKernCuda = 3 };
 
-// The kernel a launch takes, from the shape, the family override and the
-// sequences of p (n_seqs, n_kv and seqs[].k / v / len filled in).  The
-// bulk-copy kernel runs the dynamic schedule, every other kernel the static
-// one.
-DecodeKernel decode_select(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group);
+// The kernel a launch takes for a shape: the bulk-copy warp-MMA kernel
+// (claimed schedule, in-kernel merge) for 16-bit caches with 512..2048-byte
+// position rows, the CUDA-core kernel (static schedule) for the rest.
+DecodeKernel decode_select(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
 
-// Launches the selected decode kernel; returns a CUDA error code.
-cudaError_t launch_decode(const DecodeParams &p, DecodeKernel kern, bml_dtype dt, uint32_t head_dim,
-                          uint32_t group, int grid, cudaStream_t stream);
+// Launches the CUDA-core kernel; returns a CUDA error code.
+cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group, int grid,
+                          cudaStream_t stream);
 
-// Tensor-core (mma.sync m16n8k16) variant for 16-bit caches, same
-// parameters and schedule (decode_mma.cu).  launch_decode dispatches to it
-// for the shapes decode_mma_supported accepts.
-bool decode_mma_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
-cudaError_t launch_decode_mma(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
-                              int grid, cudaStream_t stream);
-
-// Same arithmetic with K/V brought in by TMA through per-sequence tensor
-// maps (decode_tma.cu); at most decode_tma_max_seqs() sequences a launch.
-// launch_decode prefers it where supported; cudaErrorNotSupported means the
-// caller should fall back.
-bool decode_tma_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
-uint32_t decode_tma_max_seqs();
-
-// Same arithmetic with tiles brought in by group bulk copies into staggered
-// shared-memory rows and chunks of tiles claimed at run time (decode_bulk.cu,
-// dynamic schedule only); 256 sequences a launch.
+// Group bulk copies into staggered shared-memory rows, warp-level MMAs, tiles
+// claimed at run time and partials merged in the same launch
+// (decode_bulk.cu); 256 sequences a launch.
 bool decode_bulk_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
 cudaError_t launch_decode_bulk(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                                int grid, cudaStream_t stream);
+// Claimed schedule: CTA b's home sequence holds tile ((2b + 1) * total) /
+// (2 * grid); this is the first CTA whose home is a sequence starting at
+// global tile `tile_begin` (the home CTAs of a sequence are a contiguous
+// range).  Home CTAs of a sequence take its first tiles and parts statically,
+// one each, so a launch issues its first copies without waiting on an atomic.
+__host__ __device__ inline uint32_t decode_home_lo(uint32_t tile_begin, uint32_t total, uint32_t grid) {
+    const uint64_t need = 2ull * grid * tile_begin;
+    if (need <= total) return 0;
+    const uint64_t num = need - total, den = 2ull * total;
+    const uint64_t b = (num + den - 1) / den;
+    return b < grid ? (uint32_t)b : grid;
+}
 
-// Kernel family for 16-bit caches.  By default (kDecodeAuto) the bulk-copy
-// kernel with the dynamic schedule; BML_DECODE_KERNEL=tma,
-// =bulk, =mma or =cuda in the environment (read once) forces the TMA, bulk-
-// copy, cp.async warp-MMA or CUDA-core kernel -- for tests and comparisons.
-enum DecodeFamily : int { kDecodeAuto = 0, kDecodeMma = 1, kDecodeCuda = 2, kDecodeBulk = 3, kDecodeTma = 4 };
-DecodeFamily decode_family_override();
-cudaError_t launch_decode_tma(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
-                              int grid, cudaStream_t stream);
+// Parts of a claimed-schedule launch (n_seqs * parts_per_seq) are limited
+// by the fixed part-tile area of a workspace.
+constexpr size_t kMaxPartTiles = 16384;
+// Partial slots a q head row of a sequence leaves per part: the consumer
+// warps serving one kv head (8 / n_kv).
+inline uint32_t decode_bulk_phases(uint32_t n_kv) { return 8u / n_kv; }
 
 // Merge of split-K slots for sequences spread over more CTAs than the
 // in-kernel merge handles well; one CTA per (sequence, head) row.

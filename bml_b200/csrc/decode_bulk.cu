@@ -1,12 +1,14 @@
 // decode_bulk.cu -- split-K flash decoding for 16-bit KV caches: group bulk
-// copies + warp-level tensor-core MMAs, with chunks of work claimed at run
-// time (sm_100a).
+// copies + warp-level tensor-core MMAs, tiles claimed at run time, partials
+// merged in the same launch (sm_100a).
 //
-// Same result and arithmetic as decode_mma.cu / decode_tma.cu (the attention
-// block of forward_layer_cached, crates/compiler/src/gguf_compiler.rs:
-// 1008-1050 in SugarFreeDoNoSo/bml, for every sequence of a batch; m16n8k16
-// MMAs with q and P as exact pairs of 16-bit terms).  What differs is how K
-// and V reach shared memory and how the work is spread over the SMs.
+// Computes, for every sequence of a batch, the attention block of
+// forward_layer_cached (crates/compiler/src/gguf_compiler.rs:1008-1050 in
+// SugarFreeDoNoSo/bml): scores q.k * scale over every cached position, a
+// max-subtracted softmax and the P.V sum for the n_heads / n_kv q heads that
+// share each kv head.  m16n8k16 MMAs take q and P as exact pairs of 16-bit
+// terms, so products are exact and sums f32 (within 1e-4 of the reference's
+// f32 / f64 arithmetic).
 //
 // Loads.  A tile of T positions of a cache ([len][n_kv][D], row_bytes =
 // n_kv*D*2 contiguous bytes per position) arrives as eight 1-D bulk copies,
@@ -15,29 +17,49 @@
 // Gc*row_bytes + 16).  The MMA row order inside a 16-position m-tile is free
 // (the softmax and P.V only need to agree on it), so m-tile mt's row r is
 // position (r % 8) * Gc + 2*mt + r / 8: the eight rows of every ldmatrix
-// come from eight different groups and hit eight different bank groups.  No
-// host-encoded tensor map (no per-length encode, 256 sequences a launch),
-// and nothing is read past a sequence's last position: the rows of a
-// partial last tile that are not copied keep stale bytes, whose scores are
-// masked and whose V elements are zeroed in the MMA fragments.
+// come from eight different groups and hit eight different bank groups.
+// Nothing is read past a sequence's last position: the rows of a partial
+// last tile that are not copied keep stale bytes, whose scores are masked
+// and whose V elements are zeroed in the MMA fragments.
 //
-// Schedule.  With a static split of the tiles, per-SM streaming rates differ
-// enough that the last CTA finishes ~40% after the median one.  Here each
-// sequence is cut into chunks of C tiles (global chunk indices); CTA b
-// starts on chunk b and claims chunk gridDim.x + (claim counter)++ each time
-// it finishes issuing one, so fast SMs take more chunks.  Every chunk leaves
-// per-warp partials (m, l, o) in its own workspace slots, so the split
-// points -- and the result, bit for bit -- do not depend on which SM took
-// which chunk; launch_slot_merge combines the slots in order.  A sequence
-// that is one chunk on one warp per head is written directly.
+// Schedule.  Per-SM streaming rates differ enough that a static split of
+// the tiles leaves the last CTA finishing ~40% after the median one, and a
+// partial per fixed-size chunk costs either balance (large chunks) or
+// partial traffic and a separate merge launch (small ones).  Here:
+//  * CTA b's home sequence holds tile (b + 1/2) * total / grid; the home CTAs
+//    of a sequence take its first tiles and its first parts statically, one
+//    each, so every CTA issues its first copy without waiting on an atomic;
+//    further tiles are claimed claim_tiles at a time from a per-sequence
+//    counter (the producer claims one claim ahead, hiding the atomic);
+//  * a CTA carries its running (m, l, o) over every tile it takes of a
+//    sequence (its "visit"); when the sequence has no unclaimed tile left it
+//    writes that carry as one part and moves to the sequence with the most
+//    unclaimed tiles, so every CTA works to the end and the tail is about
+//    one claim;
+//  * a joining visit first reserves one of the sequence's parts_per_seq part
+//    slots; a sequence that has them all taken has that many CTAs still on
+//    it, so every tile is processed by some running CTA (no CTA ever waits on
+//    one that has not started);
+//  * reservations and the done count of a sequence share one 64-bit word,
+//    so one load tells both whether the sequence is complete and how many
+//    parts it has;
+//  * when no tile is left to claim, the producer claims a merge item (a
+//    block of q-head rows of one sequence) and waits (bounded) until its
+//    sequence is complete while the consumers drain the ring; the consumers
+//    then combine that sequence's parts with the log-sum-exp rule, write
+//    the output, and claim further items one ahead.
+// Parts of a sequence depend on which CTA took which tile, so results agree
+// with the reference to the decode tolerance but may differ between runs in
+// the last bits.
 //
-// Roles (warp specialisation, no CTA-wide barrier in the main loop): warp 8
-// is the producer -- lane 0 claims chunks (one ahead, hiding the atomic's
-// latency) and arms the ring's `full` barriers, lanes 0-15 issue the group
-// copies -- over a 3-stage ring released through `empty` barriers; warps 0-7
-// consume: warp w serves kv head w % n_kv and the m-tiles w / n_kv (mod
-// 8 / n_kv) of every tile, as in decode_mma.cu, and writes its partials at
-// the end of each chunk without waiting for the other warps.
+// Roles (warp specialisation): warp 8 is the producer -- lane 0 claims tiles
+// and reserves parts, the warp picks the next sequence (one counter per
+// lane), lanes 0-15 issue the group copies -- over a 3-stage ring whose
+// stages are tiles or control records (visit start, flush, end), released
+// through `empty` barriers; warps 0-7 consume: warp w serves kv head w %
+// n_kv and the m-tiles w / n_kv (mod 8 / n_kv) of every tile, and at a flush
+// writes its own partial for its heads (8 / n_kv partial slots a part) with
+// no CTA-wide barrier.
 #include <math.h>
 
 #include "decode.cuh"
@@ -48,18 +70,21 @@ namespace bml {
 namespace {
 
 constexpr int kSmemBudget = 227 * 1024;
-constexpr int kWarps = 8;                  // consumer warps
+constexpr int kWarps = 8;                    // consumer warps
 constexpr int kThreads = (kWarps + 1) * 32;  // + the producer warp
-constexpr int kStageK = 32768;  // K bytes of a full tile (V the same), as decode.cu
+constexpr int kStageK = 32768;               // K bytes of a full tile (V the same)
 constexpr int kStages = 3;
 constexpr float kRescaleThreshold = 8.0f;
+constexpr unsigned kFull = 0xffffffffu;
+constexpr uint32_t kNone = 0xffffffffu;
 
 template <int D, int G>
 struct BCfg {
     static constexpr int NT = (2 * G + 7) / 8;  // n8 column tiles of S (4 heads each)
     static constexpr int KS = D / 16;           // k-steps of S, d-blocks of O^T
     static constexpr int MTW = 128 / D;         // m-tiles per warp per tile
-    static constexpr int SCR = 256;             // barriers, abort flag, stage info
+    static constexpr int SCR = 256;             // barriers, flags, stage records
+    static constexpr int MERGE = kWarps * (D + 4) * 4;  // merge scratch: per warp (M, L, -, -, O[D])
 };
 
 // Bytes of one K (or V) tile of T rows: eight groups at pitch
@@ -70,25 +95,223 @@ __host__ __device__ __forceinline__ uint32_t ktile_bytes_of(uint32_t T, uint32_t
 
 template <int D, int G>
 uint32_t smem_bytes(uint32_t T, uint32_t row_bytes) {
-    return kStages * 2u * ktile_bytes_of(T, row_bytes) + BCfg<D, G>::SCR + 128u;
+    return kStages * 2u * ktile_bytes_of(T, row_bytes) + BCfg<D, G>::SCR + BCfg<D, G>::MERGE + 128u;
 }
 
-// Sequence of global chunk c (binary search over the chunk ranges).
-__device__ __forceinline__ uint32_t seq_of_chunk(const DecodeParams &p, uint32_t c) {
+// Sequence holding global tile t (binary search over the tile prefix).
+__device__ __forceinline__ uint32_t seq_of_tile(const DecodeParams &p, uint32_t t) {
     uint32_t lo = 0, hi = p.n_seqs - 1;
     while (lo < hi) {
         const uint32_t mid = (lo + hi + 1) >> 1;
-        if (p.seqs[mid].tile_begin <= c) lo = mid; else hi = mid - 1;
+        if (p.seqs[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
     }
     return lo;
 }
 
-// What a filled ring stage holds, written by the producer before it arms
-// the stage's barrier and read by the consumers after their wait.
+__device__ __forceinline__ uint32_t tiles_of(const DecodeParams &p, uint32_t s) {
+    return (p.seqs[s].len + p.rows_per_tile - 1) / p.rows_per_tile;
+}
+
+// First CTA whose home is sequence s (gridDim.x past the last sequence).
+__device__ __forceinline__ uint32_t home_lo(const DecodeParams &p, uint32_t s) {
+    return s < p.n_seqs ? decode_home_lo(p.seqs[s].tile_begin, p.total_tiles, gridDim.x) : gridDim.x;
+}
+
+// Home CTAs of sequence s: they hold its first tiles and parts.
+__device__ __forceinline__ uint32_t homes_of(const DecodeParams &p, uint32_t s) {
+    return home_lo(p, s + 1) - home_lo(p, s);
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+constexpr uint32_t kNoItem = 0xffffffffu;
+
+__device__ __forceinline__ void st_release_gpu(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// One thread: claims the next merge item -- item i belongs to the (i /
+// ips)-th sequence to complete, and is block i % ips of its (row block,
+// head-dim slice) pieces -- and waits (bounded by p.wait_ns) until that
+// sequence is in the completion queue.  Returns false when every item is
+// taken, the wait gave up or the CTA is aborting; else sets item, seq and
+// np, the sequence's number of parts (home parts + joiners' reservations, at
+// most parts_per_seq).
+__device__ __noinline__ bool claim_item(const DecodeParams &p, const unsigned long long *state,
+                                           const uint32_t *queue, uint32_t ips, uint32_t items,
+                                           volatile uint32_t *abort_flag, uint32_t &item, uint32_t &seq,
+                                           uint32_t &np) {
+    if (*abort_flag) return false;
+    item = atomicAdd(&p.sched[1], 1u);
+    if (item >= items) return false;
+    uint64_t t0 = 0;
+    for (uint32_t polls = 0;; ++polls) {
+        const uint32_t v = ld_acquire_gpu(&queue[item / ips]);
+        if (v) {
+            seq = v - 1u;
+            break;
+        }
+        if (*abort_flag) return false;
+        const uint64_t now = globaltimer_ns();
+        if (!t0) t0 = now;
+        if (now - t0 > p.wait_ns) {
+            *abort_flag = 1u;
+            atomicOr(p.err, kErrTimeout);
+            return false;
+        }
+        if (polls > 8) __nanosleep(64);
+    }
+    const unsigned long long st = ld_acquire_gpu_u64(&state[seq]);
+    np = min(homes_of(p, seq) + (uint32_t)(st >> 32), p.parts_per_seq);
+    return true;
+}
+
+// This warp's share of the partial slots of RW q-head rows (qh[i]) of
+// sequence sq, for VS head dims per lane starting at dim0: slots j = sub,
+// sub + wpr, ... of the nsub = parts * nph slots, UN of them in flight per
+// lane (within the 168 registers of a 9-warp CTA), combined with the
+// log-sum-exp rule into (M, L, O) relative to M.  Empty parts (0 tiles) and
+// slots of warps that saw no valid row (m = -inf) are skipped by selection,
+// never multiplied (their bytes may be stale).
+template <int D, int VS, int RW>
+__device__ __forceinline__ void merge_share(const DecodeParams &p, uint32_t sq, const uint32_t (&qh)[RW],
+                                            uint32_t dim0, uint32_t nsub, uint32_t nph, uint32_t sub, uint32_t wpr,
+                                            int lane, float (&M)[RW], float (&L)[RW], float (&O)[RW][VS]) {
+    constexpr int UN = (VS == 4 ? 8 : VS == 2 ? 16 : 24) / RW;
+    constexpr float NEG_INF = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+        M[i] = NEG_INF;
+        L[i] = 0.f;
+#pragma unroll
+        for (int e = 0; e < VS; ++e) O[i][e] = 0.f;
+    }
+    for (uint32_t j0 = sub; j0 < nsub; j0 += (uint32_t)UN * wpr) {
+        uint32_t tl[RW][UN];
+        float2 ml[RW][UN];
+        float ov[RW][UN][VS];
+#pragma unroll
+        for (int i = 0; i < RW; ++i) {
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                const uint32_t jj = j0 + (uint32_t)u * wpr;
+                tl[i][u] = 0u;
+                if (jj < nsub) {
+                    const uint32_t prt = sq * p.parts_per_seq + jj / nph;
+                    const size_t srow = ((size_t)prt * nph + jj % nph) * p.n_heads + qh[i];
+                    tl[i][u] = __ldcg(&p.part_tiles[prt]);
+                    ml[i][u] = __ldcg(reinterpret_cast<const float2 *>(p.slot_ml + srow * 2));
+                    const float *src = p.slot_o + srow * D + dim0 + lane * VS;
+                    if constexpr (VS == 4) {
+                        const float4 x = __ldcg(reinterpret_cast<const float4 *>(src));
+                        ov[i][u][0] = x.x, ov[i][u][1] = x.y, ov[i][u][2] = x.z, ov[i][u][3] = x.w;
+                    } else if constexpr (VS == 2) {
+                        const float2 x = __ldcg(reinterpret_cast<const float2 *>(src));
+                        ov[i][u][0] = x.x, ov[i][u][1] = x.y;
+                    } else {
+                        ov[i][u][0] = __ldcg(src);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < RW; ++i) {
+#pragma unroll
+            for (int u = 0; u < UN; ++u) {
+                if (tl[i][u] == 0u || ml[i][u].x == NEG_INF) continue;
+                const float Mn = fmaxf(M[i], ml[i][u].x);
+                const float a = M[i] == NEG_INF ? 0.f : fast_exp2(M[i] - Mn);
+                const float b = fast_exp2(ml[i][u].x - Mn) * ml[i][u].y;
+                L[i] = L[i] * a + b;
+#pragma unroll
+                for (int e = 0; e < VS; ++e) O[i][e] = O[i][e] * a + ov[i][u][e] * b;
+                M[i] = Mn;
+            }
+        }
+    }
+}
+
+// Writes dims [dim0 + lane * VS, + VS) of merged row `row` (sequence-major)
+// from (M, L, O): the output O / L, and in partial mode (M, L) once per row.
+template <int D, int VS>
+__device__ __forceinline__ void merge_store(const DecodeParams &p, size_t row, uint32_t dim0, float M, float L,
+                                            const float (&O)[VS], int lane) {
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    float *dst = (p.mode == kModeFinal ? p.out : p.part_o) + row * D + dim0 + lane * VS;
+#pragma unroll
+    for (int e = 0; e < VS; ++e) dst[e] = O[e] * inv;
+    if (p.mode != kModeFinal && lane == 0 && dim0 == 0) {
+        p.part_m[row] = M;
+        p.part_l[row] = L;
+    }
+}
+
+// The consumer warps' merge of one item: R q-head rows starting at row0 of
+// sequence sq, head dims [dim0, dim0 + 32 * VS).  wpr warps share a row
+// (warp w takes row w / wpr and the slots w % wpr (mod wpr); their running
+// (M, L, O) are combined in warp order through shared memory), or, with RW
+// = 2, each warp takes two rows.  Every consumer thread calls it (the
+// combine has a named barrier).  Not inlined: its load buffers then take no
+// registers from the streaming loop.
+template <int D, int VS, int RW>
+__device__ __noinline__ void merge_item(const DecodeParams &p, uint32_t sq, uint32_t row0, uint32_t dim0,
+                                           uint32_t nsub, uint32_t nph, uint32_t wpr, int warp, int lane,
+                                           float *mscr) {
+    constexpr float NEG_INF = -INFINITY;
+    const uint32_t sub = (uint32_t)warp % wpr;
+    uint32_t qh[RW];
+#pragma unroll
+    for (int i = 0; i < RW; ++i) qh[i] = RW == 2 ? row0 + (uint32_t)warp * 2u + i : row0 + (uint32_t)warp / wpr;
+    float M[RW], L[RW], O[RW][VS];
+    merge_share<D, VS, RW>(p, sq, qh, dim0, nsub, nph, RW == 2 ? 0u : sub, RW == 2 ? 1u : wpr, lane, M, L, O);
+    if (RW == 1 && wpr > 1) {
+        float *mine = mscr + warp * (D + 4);
+        if (lane == 0) {
+            mine[0] = M[0];
+            mine[1] = L[0];
+        }
+#pragma unroll
+        for (int e = 0; e < VS; ++e) mine[4 + lane * VS + e] = O[0][e];
+        named_bar_sync(1, kWarps * 32);
+        if (sub == 0) {
+            float Mt = NEG_INF;
+            for (uint32_t i = 0; i < wpr; ++i) Mt = fmaxf(Mt, mscr[(warp + i) * (D + 4)]);
+            L[0] = 0.f;
+#pragma unroll
+            for (int e = 0; e < VS; ++e) O[0][e] = 0.f;
+            for (uint32_t i = 0; i < wpr; ++i) {
+                const float *w = mscr + (warp + i) * (D + 4);
+                const float f = w[0] == NEG_INF ? 0.f : fast_exp2(w[0] - Mt);
+                L[0] += w[1] * f;
+#pragma unroll
+                for (int e = 0; e < VS; ++e) O[0][e] += w[4 + lane * VS + e] * f;
+            }
+            M[0] = Mt;
+        }
+    }
+    if (RW == 2 || sub == 0) {
+#pragma unroll
+        for (int i = 0; i < RW; ++i)
+            merge_store<D, VS>(p, (size_t)sq * p.n_heads + qh[i], dim0, M[i], L[i], O[i], lane);
+    }
+}
+
+// Ring stage records, written by the producer before it arms the stage and
+// read by the consumers after their wait.
 struct StageInfo {
-    uint32_t seq, row0, rows, chunk, flags;
+    uint32_t kind, seq, row0, rows, part, tiles;
 };
-constexpr uint32_t kFirstOfChunk = 1u, kLastOfChunk = 2u, kEnd = 4u;
+constexpr uint32_t kTile = 0u, kVisit = 1u, kFlush = 2u, kEnd = 3u;
 
 // ----------------------------------------------------------------- kernel
 template <int D, int G, bool F16>
@@ -110,11 +333,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
     uint8_t *scr = smem + kStages * stage_bytes;
     uint64_t *full = reinterpret_cast<uint64_t *>(scr);        // [kStages]
     uint64_t *empty = full + 4;                                // [kStages]
-    volatile uint32_t *flags = reinterpret_cast<volatile uint32_t *>(full + 8);  // [0]: abort
-    volatile StageInfo *info = reinterpret_cast<volatile StageInfo *>(full + 10);  // [kStages]
+    // [0] abort, [1] merge item, [2] merge parts, [3] last CTA to leave
+    volatile uint32_t *flags = reinterpret_cast<volatile uint32_t *>(full + 8);
+    volatile StageInfo *info = reinterpret_cast<volatile StageInfo *>(full + 12);  // [kStages]
+    float *mscr = reinterpret_cast<float *>(scr + C::SCR);    // [kWarps][D + 4]
+
+    // per sequence: tiles claimed past the home tiles, and a state word whose
+    // high half counts joining visits' part reservations and low half the
+    // tiles done (8 per tile, one per consumer warp)
+    uint32_t *const claim_c = p.counters;
+    unsigned long long *const state = reinterpret_cast<unsigned long long *>(p.counters + kMaxSeqsPerLaunch);
+    uint32_t *const queue = p.counters + 3 * kMaxSeqsPerLaunch;  // completed sequences + 1, in order
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t CH = p.chunk_tiles;
+    const uint32_t nph = kWarps / p.n_kv;  // warps per kv head = partial slots per part
+    const uint32_t U = p.claim_tiles;
+    const uint32_t R = p.merge_rows, wpr = p.merge_wpr, DS = p.merge_dsplit;
+    const uint32_t ips = p.n_heads / R * DS;  // merge items per sequence
+    const uint32_t items = p.n_seqs * ips;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -128,58 +364,152 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
 
     if (warp == kWarps) {
         // ------------------------------------------------------- producer
-        // Lane 0 walks the chunks: (chunk, sequence, first tile of the chunk
-        // in the sequence, tiles in the chunk, tile within the chunk), with
-        // the next chunk claimed when the current one starts.
-        uint32_t ch = blockIdx.x, s = 0, first = 0, n = 0, j = 0, next = 0;
-        bool done = false;
-        auto start_chunk = [&]() {  // lane 0
-            if (ch >= p.total_chunks) {
-                done = true;
-                return;
-            }
-            s = seq_of_chunk(p, ch);
-            const DecodeSeq &sq = p.seqs[s];
-            first = (ch - sq.tile_begin) * CH;
-            n = min(CH, (sq.len + T - 1) / T - first);
-            j = 0;
-            next = gridDim.x + atomicAdd(&p.sched[0], 1u);
-        };
-        if (lane == 0) start_chunk();
         const uint64_t pol = l2_policy_evict_first();
-        for (uint32_t it = 0;; ++it) {
-            const uint32_t stage = it % kStages;
+        uint32_t it = 0;  // stages posted
+        // the next ring stage, once its consumers released it; false on timeout
+        auto acquire = [&](uint32_t &stage) -> bool {
+            stage = it % kStages;
             bool ok = true;
-            if (it >= (uint32_t)kStages) ok = mbar_wait(&empty[stage], ((it / kStages) - 1u) & 1u, flags, p.err);
-            if (!__all_sync(0xffffffffu, ok)) break;
-            uint32_t row0 = 0, rows = 0, seq = 0, end = 0;
+            if (it >= (uint32_t)kStages)
+                ok = mbar_wait(&empty[stage], ((it / kStages) - 1u) & 1u, flags, p.err, p.wait_ns);
+            return __all_sync(kFull, ok);
+        };
+        // a stage without data: a visit start, a flush or the end
+        auto post_ctl = [&](uint32_t kind, uint32_t seq, uint32_t part, uint32_t tiles) -> bool {
+            uint32_t stage;
+            if (!acquire(stage)) return false;
             if (lane == 0) {
-                if (done) {  // no more chunks: the consumers stop at this stage
-                    info[stage].flags = kEnd;
-                    mbar_arrive(&full[stage]);
-                    end = 1u;
-                } else {
-                    const DecodeSeq &sq = p.seqs[s];
-                    seq = s;
-                    row0 = (first + j) * T;
-                    rows = min(T, sq.len - row0);
-                    info[stage].seq = s;
-                    info[stage].row0 = row0;
-                    info[stage].rows = rows;
-                    info[stage].chunk = ch;
-                    info[stage].flags = (j == 0 ? kFirstOfChunk : 0u) | (j + 1 == n ? kLastOfChunk : 0u);
-                    mbar_arrive_expect_tx(&full[stage], 2u * rows * row_bytes);
-                    if (++j == n) {
-                        ch = next;
-                        start_chunk();
-                    }
+                info[stage].kind = kind;
+                info[stage].seq = seq;
+                info[stage].part = part;
+                info[stage].tiles = tiles;
+                mbar_arrive(&full[stage]);
+            }
+            ++it;
+            __syncwarp();
+            return true;
+        };
+        // The end record carries the CTA's first merge item, its sequence and
+        // part count, claimed and waited for here while the consumers drain
+        // the ring.
+        auto post_end = [&]() {
+            uint32_t item = kNoItem, seq = 0, np = 0;
+            if (lane == 0 && !claim_item(p, state, queue, ips, items, flags, item, seq, np)) item = kNoItem;
+            item = __shfl_sync(kFull, item, 0);
+            seq = __shfl_sync(kFull, seq, 0);
+            np = __shfl_sync(kFull, np, 0);
+            post_ctl(kEnd, item, np, seq);
+        };
+        // Warp: the sequence with the most unclaimed tiles among those worth
+        // joining (lowest index on ties), kNone if there is none.  Worth
+        // joining: a part is left, and no CTA is on it yet, or it has at
+        // least join_min unclaimed tiles (a smaller remainder is finished
+        // sooner by the CTAs already on it than a join takes).  A sequence
+        // with unclaimed tiles has every CTA that took a part of it still on
+        // it, so the rule leaves no tile behind.  The counters only grow, so a
+        // stale read never hides remaining work.
+        auto pick = [&]() -> uint32_t {
+            uint32_t cl[kMaxSeqsPerLaunch / 32], rs[kMaxSeqsPerLaunch / 32];
+#pragma unroll
+            for (int i = 0; i < kMaxSeqsPerLaunch / 32; ++i) {
+                const uint32_t s = (uint32_t)i * 32u + (uint32_t)lane;
+                cl[i] = rs[i] = 0u;
+                if (s < p.n_seqs) {
+                    cl[i] = ld_relaxed_gpu(&claim_c[s]);
+                    rs[i] = (uint32_t)(ld_relaxed_gpu_u64(&state[s]) >> 32);
                 }
             }
-            end = __shfl_sync(0xffffffffu, end, 0);
-            if (end) break;
-            seq = __shfl_sync(0xffffffffu, seq, 0);
-            row0 = __shfl_sync(0xffffffffu, row0, 0);
-            rows = __shfl_sync(0xffffffffu, rows, 0);
+            uint32_t best = kNone, best_rem = 0;
+#pragma unroll
+            for (int i = 0; i < kMaxSeqsPerLaunch / 32; ++i) {
+                if ((uint32_t)i * 32u >= p.n_seqs) break;
+                const uint32_t s = (uint32_t)i * 32u + (uint32_t)lane;
+                uint32_t rem = 0;
+                if (s < p.n_seqs) {
+                    const uint32_t nt = tiles_of(p, s), h = homes_of(p, s);
+                    const uint32_t claimed = h + cl[i];
+                    rem = (claimed < nt && h + rs[i] < p.parts_per_seq) ? nt - claimed : 0u;
+                    if (rem < p.join_min && (h > 0 || rs[i] > 0)) rem = 0u;
+                }
+                const uint32_t mx = __reduce_max_sync(kFull, rem);
+                if (mx > best_rem) {
+                    best_rem = mx;
+                    best = (uint32_t)i * 32u + (uint32_t)(__ffs(__ballot_sync(kFull, rem == mx)) - 1);
+                }
+            }
+            return best;
+        };
+
+        // visit state (lane 0's copy is the authoritative one): sequence s,
+        // part, current claim [c, c + cn), next tile j of it, tiles of the
+        // visit so far vt, prefetched next claim pref
+        uint32_t s = 0, part = 0, c = 0, cn = 0, j = 0, vt = 0, pref = 0;
+        // Warp: opens a joining visit on the best pick and posts its visit
+        // record; false if no tile is left anywhere (or on timeout).
+        auto join = [&]() -> bool {
+            for (uint32_t tries = 0; tries <= 2u * p.n_seqs + 2u; ++tries) {
+                const uint32_t cand = pick();
+                if (cand == kNone) return false;
+                uint32_t ok = 0;
+                if (lane == 0) {
+                    const uint32_t h = homes_of(p, cand), nt = tiles_of(p, cand);
+                    const uint32_t k = h + (uint32_t)(atomicAdd(&state[cand], 1ull << 32) >> 32);
+                    if (k < p.parts_per_seq) {
+                        const uint32_t cc = h + atomicAdd(&claim_c[cand], U);
+                        if (cc < nt) {  // else an empty part: its tile count stays 0
+                            ok = 1u;
+                            s = cand;
+                            part = cand * p.parts_per_seq + k;
+                            c = cc;
+                            cn = min(U, nt - c);
+                            j = 0;
+                            vt = 0;
+                            pref = h + atomicAdd(&claim_c[s], U);  // the next claim, one ahead
+                        }
+                    }
+                }
+                if (__shfl_sync(kFull, ok, 0)) {
+                    const uint32_t ss = __shfl_sync(kFull, s, 0), pp = __shfl_sync(kFull, part, 0);
+                    return post_ctl(kVisit, ss, pp, 0u);
+                }
+            }
+            return false;
+        };
+
+        bool run = (p.diag & kDiagStall) == 0u;
+        if (run) {
+            // the home visit: first tile and part by rank among the home CTAs
+            const uint32_t home = seq_of_tile(
+                p, (uint32_t)(((2ull * blockIdx.x + 1ull) * p.total_tiles) / (2ull * gridDim.x)));
+            const uint32_t r = blockIdx.x - home_lo(p, home);
+            s = home;
+            part = home * p.parts_per_seq + r;
+            c = r;
+            cn = 1;
+            j = 0;
+            vt = 0;
+            if (lane == 0) pref = homes_of(p, s) + atomicAdd(&claim_c[s], U);
+            run = post_ctl(kVisit, s, part, 0u);
+        }
+        while (run) {
+            uint32_t stage;
+            if (!acquire(stage)) break;
+            uint32_t row0 = 0, rows = 0, seq = 0, flush = 0;
+            if (lane == 0) {
+                const DecodeSeq &sq = p.seqs[s];
+                seq = s;
+                row0 = (c + j) * T;
+                rows = min(T, sq.len - row0);
+                info[stage].kind = kTile;
+                info[stage].seq = s;
+                info[stage].row0 = row0;
+                info[stage].rows = rows;
+                mbar_arrive_expect_tx(&full[stage], 2u * rows * row_bytes);
+            }
+            ++it;
+            seq = __shfl_sync(kFull, seq, 0);
+            row0 = __shfl_sync(kFull, row0, 0);
+            rows = __shfl_sync(kFull, rows, 0);
             __syncwarp();  // expected bytes are posted before any copy can complete
             // the consumers' generic-proxy reads of this stage (ordered by
             // the empty barrier) precede the async-proxy writes
@@ -195,13 +525,45 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
                                     cnt * row_bytes, &full[stage], pol);
                 }
             }
-            __syncwarp();
+            // the claim bookkeeping (which may wait on the prefetched claim)
+            // comes after the copies are on their way
+            if (lane == 0) {
+                ++j;
+                ++vt;
+                if (j == cn) {  // claim used up: the prefetched one, or the visit ends
+                    const uint32_t nt = tiles_of(p, s);
+                    if (pref < nt) {
+                        c = pref;
+                        cn = min(U, nt - c);
+                        j = 0;
+                        pref = homes_of(p, s) + atomicAdd(&claim_c[s], U);
+                    } else {
+                        flush = 1u;
+                    }
+                }
+            }
+            flush = __shfl_sync(kFull, flush, 0);
+            if (flush) {
+                const uint32_t ss = __shfl_sync(kFull, s, 0), pp = __shfl_sync(kFull, part, 0);
+                const uint32_t tt = __shfl_sync(kFull, vt, 0);
+                if (!post_ctl(kFlush, ss, pp, tt)) break;
+                if (!join()) {
+                    if (!__shfl_sync(kFull, flags[0], 0)) post_end();  // uniform: post_end is collective
+                    break;
+                }
+            }
         }
+        // After a timeout, copies of the last stages may still be landing in
+        // shared memory: wait (bounded) for them before the CTA leaves.
+        if (flags[0] && lane == 0) {
+            for (uint32_t pos = it > (uint32_t)kStages ? it - kStages : 0u; pos < it; ++pos)
+                mbar_drain(&full[pos % kStages], (pos / kStages) & 1u, p.wait_ns);
+        }
+        __syncwarp();
     } else {
         // ------------------------------------------------------- consumers
         const int g = lane >> 2, c = lane & 3;  // mma fragment row / column pair
         const int n_kv = (int)p.n_kv;
-        const int nph = kWarps / n_kv;  // warps per kv head
         const int h = warp % n_kv, ph = warp / n_kv;
 
         // q of the group as the MMA's B operand: column n = 2*head + term.
@@ -234,6 +596,44 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
             }
         };
 
+        // This warp's partial of the visit -- (m, l, o / l) of its G heads
+        // over its m-tiles -- into slot part * nph + ph; then its share of
+        // the sequence's done count.  A warp with no valid row writes m =
+        // -inf, l = 0 and zeros, never 0/0.
+        auto flush = [&](uint32_t seq, uint32_t prt, uint32_t tiles) {
+            const size_t sub = (size_t)prt * nph + (uint32_t)ph;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                float L = l_part[nt];
+                L += __shfl_xor_sync(kFull, L, 4);
+                L += __shfl_xor_sync(kFull, L, 8);
+                L += __shfl_xor_sync(kFull, L, 16);
+                const int hd = nt * 4 + c;
+                if (hd < G) {
+                    const uint32_t qh = (uint32_t)h * G + hd;
+                    const float inv = L > 0.f ? 1.f / L : 0.f;
+                    const size_t srow = sub * p.n_heads + qh;
+                    float *dst = p.slot_o + srow * D;
+#pragma unroll
+                    for (int db = 0; db < KS; ++db) {
+                        dst[db * 16 + g] = (o[nt][db][0] + o[nt][db][1]) * inv;
+                        dst[db * 16 + g + 8] = (o[nt][db][2] + o[nt][db][3]) * inv;
+                    }
+                    if (g == 0) *reinterpret_cast<float2 *>(p.slot_ml + srow * 2) = make_float2(m_run[nt], L);
+                }
+            }
+            if (lane == 0) p.part_tiles[prt] = tiles;
+            __threadfence();  // the partial is visible before the done count moves
+            __syncwarp();
+            if (lane == 0) {
+                // the warp whose count completes the sequence queues it for
+                // the merge
+                const unsigned long long old = atomicAdd(&state[seq], (unsigned long long)tiles);
+                if ((uint32_t)old + tiles == 8u * tiles_of(p, seq))
+                    st_release_gpu(&queue[atomicAdd(&p.sched[2], 1u)], seq + 1u);
+            }
+        };
+
         // byte offset of 16-byte chunk `chunk` (0 .. D/8-1) of this warp's
         // head at row r (0..15) of m-tile mt, i.e. position (r % 8) * gc +
         // 2*mt + r / 8
@@ -243,22 +643,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
         };
         auto pos_of = [&](uint32_t mt, uint32_t r) { return (r & 7u) * gc + 2u * mt + (r >> 3); };
 
-        uint32_t s = 0;
-        bool fresh = true;  // no tile of the current chunk processed yet
+        uint32_t s = 0, part = 0;
+        uint32_t end_item = kNoItem, end_np = 0, end_seq = 0;
+        bool fresh = true;  // no tile of the current visit processed yet
         for (uint32_t it = 0;; ++it) {
             const uint32_t stage = it % kStages;
-            const bool ok = mbar_wait(&full[stage], (it / kStages) & 1u, flags, p.err);
-            if (!__all_sync(0xffffffffu, ok)) break;  // timed out: leave (no barrier waits for us)
-            const uint32_t sflags = info[stage].flags;
-            if (sflags & kEnd) break;
-            const uint32_t row0 = info[stage].row0;
-            const uint32_t rows = info[stage].rows;
-            const uint32_t chunk = info[stage].chunk;
-            if (sflags & kFirstOfChunk) {  // every chunk is its own partial
-                s = info[stage].seq;
-                load_q(s);
-                fresh = true;
+            const bool ok = mbar_wait(&full[stage], (it / kStages) & 1u, flags, p.err, p.wait_ns);
+            if (!__all_sync(kFull, ok)) break;  // timed out: leave (no barrier waits for us)
+            const uint32_t kind = info[stage].kind;
+            if (kind != kTile) {
+                const uint32_t iseq = info[stage].seq, ipart = info[stage].part, itiles = info[stage].tiles;
+                if (kind == kEnd) {  // no release: nothing is posted after it
+                    end_item = iseq;
+                    end_np = ipart;
+                    end_seq = itiles;
+                    break;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[stage]);
+                if (kind == kVisit) {
+                    s = iseq;
+                    part = ipart;
+                    load_q(s);
+                    fresh = true;
+                } else {
+                    flush(s, part, itiles);
+                }
+                continue;
             }
+            const uint32_t rows = info[stage].rows;
             const uint32_t sk = smem_u32(stages + stage * stage_bytes);
             const uint32_t sv = sk + ktile_bytes;
             const bool partial = rows < T;  // rows past the end hold stale bytes
@@ -267,7 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
             float sc[MTW][NT][4];
 #pragma unroll
             for (int mw = 0; mw < MTW; ++mw) {
-                const uint32_t mt = (uint32_t)(ph + mw * nph);
+                const uint32_t mt = (uint32_t)(ph + mw * (int)nph);
                 // lane supplies row (lane & 7) + 8 * ((lane >> 3) & 1), chunk lane >> 4
                 const uint32_t a_row = (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
@@ -293,14 +706,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
                 float mx = NEG_INF;
 #pragma unroll
                 for (int mw = 0; mw < MTW; ++mw) {
-                    const uint32_t mt = (uint32_t)(ph + mw * nph);
+                    const uint32_t mt = (uint32_t)(ph + mw * (int)nph);
                     sv_[mw][nt][0] = pos_of(mt, g) < rows ? sc[mw][nt][0] + sc[mw][nt][1] : NEG_INF;
                     sv_[mw][nt][1] = pos_of(mt, g + 8) < rows ? sc[mw][nt][2] + sc[mw][nt][3] : NEG_INF;
                     mx = fmax3(mx, sv_[mw][nt][0], sv_[mw][nt][1]);
                 }
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, 16));
                 float mn = m_run[nt];
                 if (m_run[nt] == NEG_INF || mx > m_run[nt] + kRescaleThreshold) mn = fmaxf(m_run[nt], mx);
                 m_use[nt] = mn == NEG_INF ? 0.f : mn;
@@ -308,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
                 moved |= !fresh && mn != m_run[nt];
                 m_run[nt] = mn;
             }
-            if (__any_sync(0xffffffffu, moved)) {
+            if (__any_sync(kFull, moved)) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -341,7 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
             // stale bytes may hold any bit pattern, NaN included).
 #pragma unroll
             for (int mw = 0; mw < MTW; ++mw) {
-                const uint32_t mt = (uint32_t)(ph + mw * nph);
+                const uint32_t mt = (uint32_t)(ph + mw * (int)nph);
                 // lane supplies row (lane & 7) + 8 * (lane >> 4), chunk (lane >> 3) & 1
                 const uint32_t v_row = (lane & 7) + (lane >> 4) * 8;
                 // after the transpose, a[0], a[1] hold rows 2c, 2c+1 and a[2],
@@ -368,54 +781,70 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
 
             __syncwarp();  // the warp's shared-memory reads of the stage precede the release
             if (lane == 0) mbar_arrive(&empty[stage]);
-            if (!(sflags & kLastOfChunk)) continue;
+        }
 
-            // ------------- this warp's partial of the chunk: (m, l, o / l) of
-            // its G heads over its m-tiles, into slot chunk * nph + ph (or
-            // straight to the output for a one-slot sequence)
-            const DecodeSeq &sq = p.seqs[s];
-            const uint32_t slot = sq.slot_base + (chunk - sq.tile_begin) * (uint32_t)nph + (uint32_t)ph;
-            const bool single = sq.n_slots == 1;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                float L = l_part[nt];
-                L += __shfl_xor_sync(0xffffffffu, L, 4);
-                L += __shfl_xor_sync(0xffffffffu, L, 8);
-                L += __shfl_xor_sync(0xffffffffu, L, 16);
-                const int hd = nt * 4 + c;
-                if (hd < G) {
-                    const uint32_t qh = (uint32_t)h * G + hd;
-                    const float inv = L > 0.f ? 1.f / L : 0.f;  // a warp with no valid row writes zeros
-                    const size_t row = (size_t)s * p.n_heads + qh;
-                    const size_t srow = (size_t)slot * p.n_heads + qh;
-                    float *dst = single ? (p.mode == kModeFinal ? p.out : p.part_o) + row * D
-                                        : p.slot_o + srow * D;
-#pragma unroll
-                    for (int db = 0; db < KS; ++db) {
-                        dst[db * 16 + g] = (o[nt][db][0] + o[nt][db][1]) * inv;
-                        dst[db * 16 + g + 8] = (o[nt][db][2] + o[nt][db][3]) * inv;
-                    }
-                    if (g == 0) {
-                        if (!single) {
-                            p.slot_ml[srow * 2 + 0] = m_run[nt];
-                            p.slot_ml[srow * 2 + 1] = L;
-                        } else if (p.mode != kModeFinal) {
-                            p.part_m[row] = m_run[nt];
-                            p.part_l[row] = L;
-                        }
-                    }
-                }
+        // --------------------------------------------------------- merge
+        // Items in completion order: the first one claimed by the producer
+        // and passed with the end record, each further one by thread 0 after
+        // the current one.  Item piece k = item % ips of a sequence is row
+        // block k / DS (R rows) and head-dim slice k % DS (D / DS dims).
+        const uint32_t rw = R * wpr / kWarps;  // rows per warp: 1 or 2
+        if (threadIdx.x == 0) {
+            flags[1] = flags[0] ? kNoItem : end_item;
+            flags[2] = end_np;
+            flags[4] = end_seq;
+        }
+        named_bar_sync(1, kWarps * 32);
+        while (true) {
+            const uint32_t item = flags[1], np = flags[2], sq = flags[4];
+            named_bar_sync(1, kWarps * 32);  // read before thread 0 writes the next
+            if (item >= items) break;
+            const uint32_t k = item % ips;
+            const uint32_t row0 = k / DS * R, dim0 = k % DS * (D / DS);
+            const uint32_t nsub = np * nph;
+            if (rw == 2)
+                merge_item<D, D / 32, 2>(p, sq, row0, 0u, nsub, nph, 1u, warp, lane, mscr);
+            else if (DS == 1)
+                merge_item<D, D / 32, 1>(p, sq, row0, 0u, nsub, nph, wpr, warp, lane, mscr);
+            else if (DS == 2)
+                merge_item<D, D / 64, 1>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr);
+            else if constexpr (D >= 128)
+                merge_item<D, D / 128, 1>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr);
+            if (threadIdx.x == 0) {
+                uint32_t nxt = kNoItem, nseq = 0, nnp = 0;
+                if (!claim_item(p, state, queue, ips, items, flags, nxt, nseq, nnp)) nxt = kNoItem;
+                flags[1] = nxt;
+                flags[2] = nnp;
+                flags[4] = nseq;
             }
+            named_bar_sync(1, kWarps * 32);  // the next item is published; the merge scratch is free
         }
     }
 
-    // The last CTA to leave resets the claim counter for the next call.
+    // The last CTA to leave returns the schedule counters to zero for the
+    // next call.
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        if (atomicAdd(&p.sched[1], 1u) == gridDim.x - 1) {
-            p.sched[0] = 0u;
+        flags[3] = atomicAdd(&p.sched[0], 1u) == gridDim.x - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (flags[3]) {
+        __threadfence();
+        // claim counters [0, 256), state words (two u32 each) after them,
+        // merge-item claims [768, 1024)
+        for (uint32_t i = threadIdx.x; i < 4u * kMaxSeqsPerLaunch; i += blockDim.x) {
+            const uint32_t sq = i < (uint32_t)kMaxSeqsPerLaunch        ? i
+                                : i < 3u * (uint32_t)kMaxSeqsPerLaunch ? (i - kMaxSeqsPerLaunch) / 2u
+                                                                       : i - 3u * kMaxSeqsPerLaunch;
+            if (sq < p.n_seqs) p.counters[i] = 0u;
+        }
+        for (uint32_t i = threadIdx.x; i < p.n_seqs * p.parts_per_seq; i += blockDim.x) p.part_tiles[i] = 0u;
+        __syncthreads();
+        if (threadIdx.x == 0) {
             p.sched[1] = 0u;
+            p.sched[2] = 0u;
+            p.sched[0] = 0u;
             __threadfence();
         }
     }
@@ -450,35 +879,49 @@ cudaError_t launch_g(const DecodeParams &p, uint32_t group, int grid, cudaStream
     }
 }
 
-template <int D>
-uint32_t smem_for_group(uint32_t group, uint32_t T, uint32_t row_bytes) {
-    switch (group) {
-        case 1: return smem_bytes<D, 1>(T, row_bytes);
-        case 2: return smem_bytes<D, 2>(T, row_bytes);
-        case 4: return smem_bytes<D, 4>(T, row_bytes);
-        default: return smem_bytes<D, 8>(T, row_bytes);
-    }
-}
-
 }  // namespace
 
 bool decode_bulk_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group) {
-    // the warp layout of decode_mma.cu, and the padded ring within 227 KB
-    if (!decode_mma_supported(dt, head_dim, n_kv, group)) return false;
-    const uint32_t T = decode_rows_per_tile(dt, head_dim, n_kv);
-    const uint32_t row_bytes = n_kv * head_dim * 2u;
-    const uint32_t smem = head_dim == 128 ? smem_for_group<128>(group, T, row_bytes)
-                                          : smem_for_group<64>(group, T, row_bytes);
+    if (dt != BML_BF16 && dt != BML_F16) return false;
+    if (head_dim != 64 && head_dim != 128) return false;
+    if (group != 1 && group != 2 && group != 4 && group != 8) return false;
+    if (n_kv != 1 && n_kv != 2 && n_kv != 4 && n_kv != 8) return false;
+    // whole m-tiles: T = 32 KiB / row_bytes must be a multiple of 16 and
+    // split evenly over the 8 / n_kv warps of a kv head
+    const uint32_t row_bytes = n_kv * head_dim * 2;
+    if (row_bytes < 512 || row_bytes > 2048) return false;
+    const uint32_t T = kStageK / row_bytes;
+    if (T % 16 != 0 || (T / 16) % (kWarps / n_kv) != 0) return false;
+    const uint32_t smem = head_dim == 128 ? smem_bytes<128, 8>(T, row_bytes) : smem_bytes<64, 8>(T, row_bytes);
     return smem <= (uint32_t)kSmemBudget;
 }
 
 cudaError_t launch_decode_bulk(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group, int grid,
                                cudaStream_t stream) {
     if (!decode_bulk_supported(dt, head_dim, p.n_kv, group)) return cudaErrorNotSupported;
-    if (p.rows_per_tile * p.row_bytes > (uint32_t)kStageK || p.row_bytes % 128 != 0 || p.rows_per_tile % 16 != 0)
+    if (p.rows_per_tile * p.row_bytes != (uint32_t)kStageK || p.row_bytes % 128 != 0 || p.rows_per_tile % 16 != 0)
         return cudaErrorInvalidValue;
-    // dynamic schedule only: every CTA starts on chunk blockIdx.x
-    if (p.chunk_tiles == 0 || !p.sched || grid <= 0 || (uint32_t)grid > p.total_chunks) return cudaErrorInvalidValue;
+    // every CTA starts on a tile; parts, merge items and counters in range
+    if (!p.sched || !p.part_tiles || !p.counters || grid <= 0 || (uint32_t)grid > p.total_tiles ||
+        p.n_seqs == 0 || p.n_seqs > (uint32_t)kMaxSeqsPerLaunch || p.parts_per_seq == 0 ||
+        (size_t)p.n_seqs * p.parts_per_seq > kMaxPartTiles || p.claim_tiles == 0)
+        return cudaErrorInvalidValue;
+    // merge items: wpr warps per row and 1 or 2 rows per warp (2 only with
+    // one warp per row), whole items per sequence
+    const uint32_t wpr = p.merge_wpr, R = p.merge_rows;
+    const uint32_t DS = p.merge_dsplit;
+    if (!(wpr == 1 || wpr == 2 || wpr == 4 || wpr == 8) || !(R * wpr == (uint32_t)kWarps ||
+                                                            (wpr == 1 && R == 2u * kWarps)) ||
+        p.n_heads % R != 0 || !(DS == 1 || DS == 2 || DS == 4) || 32u * DS > head_dim ||
+        (DS > 1 && R * wpr != (uint32_t)kWarps))
+        return cudaErrorInvalidValue;
+    // every home CTA's static part fits the parts of its sequence
+    for (uint32_t s = 0; s < p.n_seqs; ++s) {
+        const uint32_t lo = decode_home_lo(p.seqs[s].tile_begin, p.total_tiles, (uint32_t)grid);
+        const uint32_t hi = s + 1 < p.n_seqs ? decode_home_lo(p.seqs[s + 1].tile_begin, p.total_tiles, (uint32_t)grid)
+                                             : (uint32_t)grid;
+        if (hi - lo > p.parts_per_seq) return cudaErrorInvalidValue;
+    }
     const bool f16 = dt == BML_F16;
     if (head_dim == 128) return f16 ? launch_g<128, true>(p, group, grid, stream) : launch_g<128, false>(p, group, grid, stream);
     return f16 ? launch_g<64, true>(p, group, grid, stream) : launch_g<64, false>(p, group, grid, stream);

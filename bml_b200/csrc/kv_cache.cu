@@ -111,11 +111,11 @@ __global__ void softmax_kernel(const float *__restrict__ x, uint32_t n, float *_
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) orow[i] = ok ? orow[i] / sum : inv_n;
 }
 
-__global__ void diag_exp2_kernel(const float2 *__restrict__ x, uint32_t n2, int method, float2 *__restrict__ out) {
+__global__ void diag_exp2_kernel(const float2 *__restrict__ x, uint32_t n2, float2 *__restrict__ out) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n2) return;
     const float2 v = x[i];
-    out[i] = method == 1 ? exp2_poly2(v) : make_float2(fast_exp2(v.x), fast_exp2(v.y));
+    out[i] = make_float2(fast_exp2(v.x), fast_exp2(v.y));
 }
 
 // RoPE of gguf_compiler.rs:1290-1317 (interleaved pairs (2i, 2i+1) of each
@@ -273,10 +273,10 @@ cudaError_t kv_rope_append(float *q, uint32_t n_heads, const float *k, const flo
     return cudaGetLastError();
 }
 
-cudaError_t diag_exp2(const float *x, uint32_t n, int method, float *out, cudaStream_t st) {
+cudaError_t diag_exp2(const float *x, uint32_t n, float *out, cudaStream_t st) {
     if (n == 0) return cudaSuccess;
     const uint32_t n2 = n / 2;
-    diag_exp2_kernel<<<(n2 + 255) / 256, 256, 0, st>>>(reinterpret_cast<const float2 *>(x), n2, method,
+    diag_exp2_kernel<<<(n2 + 255) / 256, 256, 0, st>>>(reinterpret_cast<const float2 *>(x), n2,
                                                         reinterpret_cast<float2 *>(out));
     return cudaGetLastError();
 }

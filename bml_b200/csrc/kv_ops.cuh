@@ -30,7 +30,7 @@ cudaError_t kv_rope_append_rows(const AppendRows &p, uint32_t n_seqs, float *q, 
                                 bml_dtype dst_t, cudaStream_t st);
 cudaError_t kv_rope_append(float *q, uint32_t n_heads, const float *k, const float *v, void *kd, void *vd,
                            bml_dtype dst_t, uint32_t n_kv, uint32_t d, uint32_t pos, cudaStream_t st);
-cudaError_t diag_exp2(const float *x, uint32_t n, int method, float *out, cudaStream_t st);
+cudaError_t diag_exp2(const float *x, uint32_t n, float *out, cudaStream_t st);
 cudaError_t softmax_rows(const float *x_dev, uint32_t n_rows, uint32_t n, float *out_dev, cudaStream_t st);
 
 }  // namespace bml

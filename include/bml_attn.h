@@ -246,24 +246,34 @@ bml_status bml_attn_decode_batched(const bml_seq_desc *seqs_host,
  * device-wide synchronisation would stall other streams.  It takes no
  * workspace; its scratch is a fixed 4 MiB array in device global memory
  * that every GPU loading this library holds until the process exits, and it
- * allocates nothing itself.  A call whose smallest usable scratch -- split
- * slots for 2 * n_seqs + (SM count) partial results of n_heads rows of
- * head_dim + 2 floats, plus 8.5 KiB of tickets -- is above 4 MiB (e.g. 256
- * sequences of 64 heads at head_dim 128) returns BML_E_INVALID; below that
- * the kernels size their work to the slots the array holds.  The
+ * allocates nothing itself.  A call whose smallest usable scratch -- partial
+ * slots for max(2 * n_seqs + (SM count), (8 / n_kv_heads) * n_seqs) results of n_heads rows
+ * of head_dim + 2 floats, plus 72.25 KiB of counters -- is above 4 MiB (e.g.
+ * 256 sequences of 64 heads at head_dim 128) returns BML_E_INVALID; below
+ * that the kernels size their work to the slots the array holds.  The
  * first call on a device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call before any stream capture.
  * All calls share the one array, which keeps the last call's contents: each
- * call first clears the merge tickets and error word on `stream`, so calls
- * that overlap in time on the GPU race with each other and must be
- * serialised (one stream, or events between streams).  Results equal
- * bml_attn_decode_batched's.  Asynchronous. */
+ * call first clears the schedule counters on `stream`, so calls that
+ * overlap in time on the GPU race with each other and must be serialised
+ * (one stream, or events between streams).  The array's error word is not
+ * cleared by a call: a bounded device wait that gave up stays recorded
+ * until bml_attn_noalloc_check reads it.  Results agree with
+ * bml_attn_decode_batched's within the decode tolerance.  Asynchronous. */
 bml_status bml_attn_decode_batched_noalloc(const bml_seq_desc *seqs_host,
                                            uint32_t n_seqs, uint32_t n_heads,
                                            uint32_t n_kv_heads, uint32_t head_dim,
                                            bml_dtype kv_dtype, float scale,
                                            const float *q_dev, float *out_dev,
                                            void *stream);
+
+/* Reads and clears the error word of the fixed scratch array of
+ * bml_attn_decode_batched_noalloc on the current device: BML_E_TIMEOUT if a
+ * bounded device wait of an earlier call gave up (that call's output is not
+ * valid), else BML_OK.  Like the entry point it serves, it has no
+ * counterpart in the reference and allocates nothing.  Synchronises
+ * `stream`. */
+bml_status bml_attn_noalloc_check(void *stream);
 
 /* KV-split partial: the same computation over each sequence's slice of the
  * cache, returning per (sequence, q head) the running max m (in log2
@@ -332,18 +342,6 @@ bml_status bml_attn_prefill(const void *q_dev, const void *k_dev,
  * Asynchronous. */
 bml_status bml_softmax_f32(const float *x_dev, uint32_t n_rows, uint32_t n,
                            float *out_dev, void *stream);
-
-/* ------------------------------------------------------------------------ */
-/* Diagnostics                                                              */
-/* ------------------------------------------------------------------------ */
-
-/* Evaluates 2^x with one of the device exponentials the attention kernels
- * use, so tests can bound their error: method 0 = the SFU (ex2.approx),
- * method 1 = the FMA-pipe polynomial the prefill softmax uses for part of
- * its exponentials.  No reference counterpart.  n must be even.
- * Asynchronous. */
-bml_status bml_diag_exp2(const float *x_dev, uint32_t n, int method,
-                         float *out_dev, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Device-side error word                                                   */

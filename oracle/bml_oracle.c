@@ -452,6 +452,51 @@ int orc_attn_prefill(const float *q, const void *k, const void *v, int dtype,
 }
 
 /*
+ * Prefill at query rows chosen by the caller: row r of the result is query
+ * position rows[2r + 1] of sequence rows[2r], for q heads [h_lo, h_hi).
+ * Each row is the same per-token causal attention as orc_attn_prefill
+ * (gguf_compiler.rs:946-958 over :1008-1050), and rows do not depend on one
+ * another, so a subset gives exactly the values of the full loop.
+ * out: [n_rows][h_hi - h_lo][head_dim] f64.  Parallel over (row, head).
+ */
+int orc_attn_prefill_rows(const float *q, const void *k, const void *v, int dtype,
+                          uint32_t n_seqs, uint32_t seq_len, uint32_t n_heads,
+                          uint32_t n_kv, uint32_t head_dim, double scale,
+                          const uint32_t *rows, uint32_t n_rows, uint32_t h_lo,
+                          uint32_t h_hi, double *out, int n_threads) {
+    uint32_t g = orc_group(n_heads, n_kv);
+    if (!g || head_dim == 0 || seq_len == 0 || h_lo >= h_hi || h_hi > n_heads) return -1;
+    for (uint32_t r = 0; r < n_rows; ++r)
+        if (rows[2 * r] >= n_seqs || rows[2 * r + 1] >= seq_len) return -1;
+    if (scale < 0) scale = 1.0 / sqrt((double)head_dim);
+    size_t es = dtype == ORC_F32 ? 4 : 2;
+    size_t kv_seq_elems = (size_t)seq_len * n_kv * head_dim;
+    uint32_t nh = h_hi - h_lo;
+    long total = (long)n_rows * nh;
+#ifdef _OPENMP
+    if (n_threads < 1) n_threads = omp_get_max_threads();
+#pragma omp parallel num_threads(n_threads) if (n_threads > 1)
+#endif
+    {
+        float *scores = (float *)malloc((size_t)seq_len * sizeof(float));
+#ifdef _OPENMP
+#pragma omp for schedule(dynamic, 4)
+#endif
+        for (long w = 0; w < total; ++w) {
+            uint32_t r = (uint32_t)(w / nh), h = h_lo + (uint32_t)(w % nh);
+            uint32_t s = rows[2 * r], t = rows[2 * r + 1];
+            const char *ks = (const char *)k + (size_t)s * kv_seq_elems * es;
+            const char *vs = (const char *)v + (size_t)s * kv_seq_elems * es;
+            size_t qo = (((size_t)s * seq_len + t) * n_heads + h) * head_dim;
+            orc_attn_one_head(q + qo, ks, vs, dtype, seq_len, n_kv, head_dim, h / g, t, scale, scores,
+                              out + ((size_t)r * nh + (h - h_lo)) * head_dim);
+        }
+        free(scores);
+    }
+    return 0;
+}
+
+/*
  * The reference's literal access pattern for one decode token
  * (gguf_compiler.rs:1026-1049): a fresh heap copy for every load_k, and for
  * every load_v inside the head_dim loop, which makes the loop O(H*d*d*L).

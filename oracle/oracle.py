@@ -72,6 +72,9 @@ def lib():
             L.orc_attn_prefill.restype = i32
             L.orc_attn_prefill.argtypes = [vp, vp, vp, i32, u32, u32, u32, u32, u32,
                                            C.c_double, u32, u32, f64p, i32]
+            L.orc_attn_prefill_rows.restype = i32
+            L.orc_attn_prefill_rows.argtypes = [vp, vp, vp, i32, u32, u32, u32, u32, u32, C.c_double, vp,
+                                                u32, u32, u32, f64p, i32]
             L.orc_attn_decode_literal.restype = i32
             L.orc_attn_decode_literal.argtypes = [vp, vp, vp, u32, u32, u32, u32, u32, u32,
                                                   u32, f64p]
@@ -264,6 +267,26 @@ def attn_prefill(q, k, v, scale=-1.0, rows=None, dtype=None, n_threads=0) -> np.
     out = np.full(q.shape, np.nan, np.float64)
     rc = lib().orc_attn_prefill(_ptr(q), _ptr(k), _ptr(v), code, n_seqs, S, n_heads, n_kv, d,
                                 float(scale), lo, hi, _ptr(out), n_threads)
+    if rc != 0:
+        raise ValueError("rejected shape")
+    return out
+
+
+def attn_prefill_rows(q, k, v, rows, heads=None, scale=-1.0, dtype=None, n_threads=0) -> np.ndarray:
+    """Causal prefill at chosen query rows: rows is a list of (sequence,
+    position); returns [len(rows), h_hi - h_lo, d] for heads=(h_lo, h_hi)
+    (default all), the values attn_prefill gives at those rows."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k)
+    v = np.ascontiguousarray(v)
+    code = dtype if dtype is not None else _dtype_code(k)
+    n_seqs, S, n_heads, d = q.shape
+    n_kv = k.shape[2]
+    h_lo, h_hi = heads if heads is not None else (0, n_heads)
+    r = np.ascontiguousarray(np.asarray(rows, dtype=np.uint32).reshape(-1, 2))
+    out = np.empty((r.shape[0], h_hi - h_lo, d), np.float64)
+    rc = lib().orc_attn_prefill_rows(_ptr(q), _ptr(k), _ptr(v), code, n_seqs, S, n_heads, n_kv, d,
+                                     float(scale), _ptr(r), r.shape[0], h_lo, h_hi, _ptr(out), n_threads)
     if rc != 0:
         raise ValueError("rejected shape")
     return out

@@ -1,5 +1,5 @@
 """The C ABI: the library loads, exports exactly what include/*.h
-(bml_attn.h, bml_weights.h, bml_gguf.h) declares, and rejects bad arguments on the host
+(bml_attn.h, bml_weights.h, bml_gguf.h and the test-only bml_diag.h) declares, and rejects bad arguments on the host
 (no GPU needed: nothing is launched before validation passes)."""
 import ctypes as C
 import os
@@ -9,7 +9,8 @@ import subprocess
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("bml_attn.h", "bml_weights.h", "bml_gguf.h")]
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("bml_attn.h", "bml_weights.h", "bml_gguf.h",
+                                                      "bml_diag.h")]
 
 
 def declared_functions():

@@ -159,18 +159,24 @@ def test_partial_then_merge_equals_full(cuda):
     assert np.abs(merged.cpu().numpy() - want).max() < TOL
 
 
-def test_repeat_calls_identical_and_no_timeout(cuda):
-    """The workspace's merge tickets reset themselves: a second call gives
-    bit-identical results, and no bounded wait gave up."""
+def test_repeat_calls_agree_and_no_timeout(cuda):
+    """The workspace's schedule counters reset themselves: repeated calls on
+    one workspace all match the oracle, agree with each other to 1e-5 (which
+    SM takes which tile varies between calls, so the parts of a sequence --
+    and the last bits of its result -- may differ), and no bounded wait gave
+    up."""
     import bml_b200
     q, ks, vs = W.batched_tinyllama(n_seqs=16)
+    want = oracle.attn_decode_batched(q, ks, vs)
     qd = to_dev(q)
     b = bml_b200.SeqBatch([to_dev(k) for k in ks], [to_dev(v) for v in vs])
     ws = bml_b200.Workspace()
     a = bml_b200.decode_batched(qd, b, workspace=ws).clone()
-    c = bml_b200.decode_batched(qd, b, workspace=ws)
-    torch.cuda.synchronize()
-    assert torch.equal(a, c)
+    for _ in range(5):
+        c = bml_b200.decode_batched(qd, b, workspace=ws)
+        torch.cuda.synchronize()
+        assert (a - c).abs().max().item() < 1e-5
+        assert np.abs(c.cpu().numpy() - want).max() < TOL
     ws.check()
 
 
@@ -278,8 +284,8 @@ def test_gpu_softmax_f32(cuda):
 
 
 def test_long_and_short_sequences_mixed(cuda):
-    """Long sequences span many CTAs (their split-K slots are merged by the
-    separate merge kernel) next to short ones handled by a single CTA."""
+    """Long sequences span many CTAs (many parts, merged by several warps per
+    row) next to short ones handled by a single CTA (one part)."""
     rng = np.random.default_rng(31)
     lens = [60000, 3, 20000, 1, 129]
     q = rng.standard_normal((len(lens), 32, 128), dtype=np.float32)

@@ -175,3 +175,16 @@ def test_golden_fixtures():
 
 def test_batched_lengths_match_survey_sum():
     assert int(W.batched_lengths().sum()) == 143173
+
+
+def test_prefill_rows_subset_equals_full_loop():
+    """attn_prefill_rows (any subset of query rows and heads) gives exactly
+    the values of the full per-token loop at those rows."""
+    rng = np.random.default_rng(12)
+    q = rng.standard_normal((3, 70, 8, 64), dtype=np.float32)
+    k = rng.standard_normal((3, 70, 2, 64), dtype=np.float32)
+    v = rng.standard_normal((3, 70, 2, 64), dtype=np.float32)
+    full = oracle.attn_prefill(q, k, v)
+    rows = [(0, 0), (2, 69), (1, 33), (0, 64), (2, 1)]
+    got = oracle.attn_prefill_rows(q, k, v, rows, heads=(3, 7))
+    np.testing.assert_array_equal(got, np.stack([full[s, t, 3:7] for s, t in rows]))

@@ -5,12 +5,17 @@ allocator owns all device memory, or a serving loop that must not pay
 cudaMalloc's device-wide synchronisation -- and takes its scratch from the
 library's fixed 4 MiB device array.  These tests call it through the C ABI
 and check it against bml_attn_decode_batched (the workspace-taking entry
-point) on two calls in a row, and that oversized batches are refused."""
+point) on two calls in a row, against the oracle on the 64-sequence ragged
+TinyLlama-shaped batch, that bml_attn_noalloc_check reports no timeout
+after good calls, and that oversized batches are refused."""
 import ctypes as C
 
 import numpy as np
 import pytest
 import torch
+
+import oracle
+from bml_b200 import workloads as W
 
 pytestmark = pytest.mark.gpu
 
@@ -47,6 +52,29 @@ def test_noalloc_matches_workspace_entry_point(cuda, lens, n_kv, d, group, dtype
         torch.cuda.synchronize()
         err = (out - want).abs().max().item()
         assert err < TOL, err
+    assert L.lib().bml_attn_noalloc_check(stream) == L.BML_OK, L.last_error()
+
+
+def test_noalloc_matches_oracle_on_ragged_batch(cuda):
+    """64 sequences of U[128, 4096] positions (seed 2), f16 KV, 32 q / 4 kv
+    heads, d = 64: two calls in a row against the oracle, then the check."""
+    import bml_b200
+    import bml_b200._lib as L
+    from bml_b200.attention import dtype_code
+    q, ks, vs = W.batched_tinyllama()
+    want = oracle.attn_decode_batched(q, ks, vs)
+    batch = bml_b200.SeqBatch([torch.from_numpy(k).cuda() for k in ks], [torch.from_numpy(v).cuda() for v in vs])
+    qd = torch.from_numpy(q).cuda()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        out = torch.full_like(qd, float("nan"))
+        st = L.lib().bml_attn_decode_batched_noalloc(batch.descs, len(batch), 32, 4, 64, dtype_code(torch.float16),
+                                                     -1.0, C.c_void_p(qd.data_ptr()), C.c_void_p(out.data_ptr()),
+                                                     stream)
+        assert st == L.BML_OK, L.last_error()
+        err = np.abs(out.cpu().numpy() - want).max()
+        assert err < TOL, err
+    assert L.lib().bml_attn_noalloc_check(stream) == L.BML_OK, L.last_error()
 
 
 def test_noalloc_refuses_batches_beyond_its_scratch(cuda):
