@@ -679,7 +679,7 @@ def run_longctx_obj(dev, steps, warmup, dist, peaks, cpu_budget):
     ws = bml_b200.Workspace(dev).ensure(1, H, d)
     merged = torch.empty(1, H, d, dtype=torch.float32, device=dev)
     step = sharding.KVSplitDecode(dist.pg, dist.world, H, d, dev)
-    fn = lambda: step(q, batch, ws, out=merged)  # noqa: E731
+    fn = lambda: step(q, batch, ws, out=merged, total_len=total_len)  # noqa: E731
     fn()
     torch.cuda.synchronize()
     ms, clocks = timed_loop(fn, steps, warmup, dist, dist.local)

@@ -14,7 +14,24 @@ attention runs in one thread of one process):
 """
 from __future__ import annotations
 
+import time
 from typing import Callable, Sequence
+
+
+class RankFailure(RuntimeError):
+    """A peer rank of a KV-split decode stopped answering: it missed a
+    health check within the timeout, or a collective with it failed.  The
+    reference's counterpart is its worker HealthCheck message
+    (crates/runtime/src/net.rs) and the CLI's exit on a TCP error."""
+
+    def __init__(self, msg: str, rank: int | None = None):
+        super().__init__(msg)
+        self.rank = rank
+
+
+class SplitMismatch(RuntimeError):
+    """The ranks of a KV-split decode disagree on the split (world size,
+    head shape or total KV length), so their partials would not merge."""
 
 
 def lpt_partition(lengths: Sequence[int], n_parts: int) -> list[list[int]]:
@@ -58,15 +75,33 @@ class KVSplitDecode:
 
     `pg` is the torch.distributed module (or None for one rank).  The
     partial and merge backends default to the CUDA library; tests on CPU
-    pass restatements instead, so the exchange logic runs under gloo."""
+    pass restatements instead, so the exchange logic runs under gloo.
+
+    Failure detection (all on the host; nothing waits on the GPU):
+    * the first call checks that every rank has the same plan (world size,
+      q heads, head_dim, total KV length); SplitMismatch otherwise;
+    * health_check(), called by every rank between steps (the same number of
+      times), publishes this rank's check count in the process group's
+      key-value store and waits (bounded) until every peer has published
+      the same count; RankFailure names a peer that did not answer in time;
+    * a collective that fails (a peer left, or the process group's own
+      timeout ran out) is raised as RankFailure.
+    """
 
     def __init__(self, pg, world: int, n_heads: int, head_dim: int, device,
-                 partial_fn: Callable | None = None, merge_fn: Callable | None = None):
+                 partial_fn: Callable | None = None, merge_fn: Callable | None = None,
+                 store=None, health_timeout_s: float = 10.0):
         import torch
         self.pg, self.world, self.n_heads, self.d = pg, world, n_heads, head_dim
         self.device = device
         self.partial_fn = partial_fn
         self.merge_fn = merge_fn
+        self.store = store
+        self.health_timeout_s = health_timeout_s
+        self.rank = pg.get_rank() if pg is not None and world > 1 else 0
+        self.steps = 0
+        self._checks = 0
+        self._plan_checked = world == 1
         self._packed = None
         self._gathered = None
         self._torch = torch
@@ -79,13 +114,72 @@ class KVSplitDecode:
             self._gathered = torch.empty(self.world * size, dtype=torch.float32, device=self.device)
         return self._packed, self._gathered
 
-    def __call__(self, q, batch, workspace=None, out=None):
+    def _collective(self, what: str, fn, *args):
+        try:
+            return fn(*args)
+        except (RuntimeError, ValueError, OSError) as e:  # gloo / NCCL errors, timeouts
+            raise RankFailure(f"rank {self.rank}: {what} failed ({type(e).__name__}: {e})") from e
+
+    def check_plan(self, total_len: int) -> None:
+        """All ranks agree on (world, n_heads, head_dim, total_len)."""
+        torch = self._torch
+        mine = torch.tensor([self.world, self.n_heads, self.d, int(total_len)], dtype=torch.int64,
+                            device=self.device)
+        every = torch.empty(self.world * 4, dtype=torch.int64, device=self.device)
+        self._collective("plan all-gather", self.pg.all_gather_into_tensor, every, mine)
+        rows = every.view(self.world, 4).cpu().tolist()
+        if any(r != rows[0] for r in rows):
+            raise SplitMismatch(f"rank {self.rank}: split plans differ across ranks "
+                                f"(world, n_heads, head_dim, total_len): {rows}")
+        self._plan_checked = True
+
+    def _store(self):
+        if self.store is not None:
+            return self.store
+        from torch.distributed import distributed_c10d as c10d
+        return c10d._get_default_store()
+
+    def health_check(self, timeout_s: float | None = None) -> None:
+        """Publishes this rank's health-check count and waits until every
+        peer has published at least the same count (each call needs a fresh
+        answer from every peer); RankFailure names the first peer still
+        missing when the timeout runs out."""
+        if self.world == 1:
+            return
+        self._checks += 1
+        store = self._store()
+        deadline = time.monotonic() + (self.health_timeout_s if timeout_s is None else timeout_s)
+        pending = [r for r in range(self.world) if r != self.rank]
+        try:
+            store.set(f"bml/kvsplit/{self.rank}", str(self._checks))
+        except (RuntimeError, OSError) as e:  # the store's host rank is gone
+            raise RankFailure(f"rank {self.rank}: key-value store unreachable ({e})", rank=0) from e
+        while pending:
+            still = []
+            for r in pending:
+                key = f"bml/kvsplit/{r}"
+                try:
+                    seen = store.check([key]) and int(store.get(key).decode()) >= self._checks
+                except (RuntimeError, OSError) as e:
+                    raise RankFailure(f"rank {self.rank}: key-value store unreachable ({e})", rank=0) from e
+                if not seen:
+                    still.append(r)
+            pending = still
+            if pending and time.monotonic() > deadline:
+                raise RankFailure(f"rank {self.rank}: rank {pending[0]} missed health check {self._checks} "
+                                  f"(after {self.steps} steps)", rank=pending[0])
+            if pending:
+                time.sleep(0.01)
+
+    def __call__(self, q, batch, workspace=None, out=None, total_len: int | None = None):
         torch = self._torch
         if self.world == 1 and self.partial_fn is None and self.merge_fn is None:
-            # one rank holds the whole sequence: the plain decode, whose slot
-            # merge already yields the final output (no partial, no merge)
+            # one rank holds the whole sequence: the plain decode, whose
+            # in-kernel merge already yields the final output
             from .attention import decode_batched
             return decode_batched(q, batch, out=out, workspace=workspace)
+        if not self._plan_checked:
+            self.check_plan(total_len if total_len is not None else -1)
         n_seqs = q.shape[0]
         n_rows = n_seqs * self.n_heads
         packed, gathered = self._buffers(n_rows)
@@ -98,7 +192,7 @@ class KVSplitDecode:
         else:
             self.partial_fn(q, batch, m, l_, o)
         if self.world > 1:
-            self.pg.all_gather_into_tensor(gathered, packed)
+            self._collective("partials all-gather", self.pg.all_gather_into_tensor, gathered, packed)
             parts = gathered.view(self.world, -1)
         else:
             parts = packed.view(1, -1)
@@ -109,4 +203,5 @@ class KVSplitDecode:
             merge_lse_packed(parts, n_rows, self.d, out=out)
         else:
             self.merge_fn(parts, n_rows, self.d, out)
+        self.steps += 1
         return out

@@ -148,3 +148,96 @@ def test_batched_sharding_is_consistent_across_ranks():
         a, b = ret[0], ret[1]
     assert sorted(a[0] + b[0]) == list(range(64))
     assert a[1] == b[1] == sum(lens)
+
+
+# ---------------------------------------------------------------------------
+# Failure detection on the host (no GPU involved): a rank that leaves between
+# steps, and ranks that disagree on the split.
+# ---------------------------------------------------------------------------
+def _failure_worker(rank, world, port, mode, q, k, v, ret):
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    total = k.shape[0] + (rank if mode == "mismatch" else 0)  # a rank with a different length
+    lo, hi = sharding.kv_split_ranges(k.shape[0], world)[rank]
+    scale = 1.0 / np.sqrt(q.shape[-1])
+
+    def partial_fn(qq, batch, m, l_, o):
+        mm, ll, oo = np_partial(q[0], batch[0], batch[1], scale)
+        m.copy_(torch.from_numpy(mm).view_as(m))
+        l_.copy_(torch.from_numpy(ll).view_as(l_))
+        o.copy_(torch.from_numpy(oo).view_as(o))
+
+    step = sharding.KVSplitDecode(dist, world, q.shape[1], q.shape[2], torch.device("cpu"),
+                                  partial_fn=partial_fn, merge_fn=np_merge_packed, health_timeout_s=3.0)
+    try:
+        if mode == "mismatch":
+            try:
+                step(torch.from_numpy(q), (k[lo:hi], v[lo:hi]), total_len=total)
+                ret[rank] = ("no error",)
+            except sharding.SplitMismatch as e:
+                ret[rank] = ("SplitMismatch", str(e))
+            return
+        # mode "leave": one good step with a health check on both ranks
+        step(torch.from_numpy(q), (k[lo:hi], v[lo:hi]), total_len=total)
+        step.health_check()
+        if rank == 1:
+            ret[1] = ("left",)
+            os._exit(0)  # leaves between steps: nothing of it is in flight
+        t0 = time.monotonic()
+        try:
+            step.health_check()
+            hc = ("no error", time.monotonic() - t0)
+        except sharding.RankFailure as e:
+            hc = ("RankFailure", time.monotonic() - t0, e.rank)
+        t0 = time.monotonic()
+        try:
+            step(torch.from_numpy(q), (k[lo:hi], v[lo:hi]), total_len=total)
+            st = ("no error", time.monotonic() - t0)
+        except sharding.RankFailure as e:
+            st = ("RankFailure", time.monotonic() - t0)
+        ret[0] = (hc, st)
+    finally:
+        if mode == "leave":
+            os._exit(0)  # the group has lost a rank: leave without a collective teardown
+        dist.destroy_process_group()
+
+
+def _run_failure(mode):
+    rng = np.random.default_rng(5)
+    L, n_kv, d, H = 300, 2, 32, 8
+    q = rng.standard_normal((1, H, d), dtype=np.float32)
+    k = rng.standard_normal((L, n_kv, d), dtype=np.float32)
+    v = rng.standard_normal((L, n_kv, d), dtype=np.float32)
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        ret = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_failure_worker, args=(r, 2, port, mode, q, k, v, ret)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(90)
+            if p.is_alive():
+                p.kill()
+                pytest.fail(f"{mode}: a rank did not finish within 90 s")
+        return dict(ret)
+
+
+def test_rank_that_leaves_is_detected_within_the_timeout():
+    """Rank 1 leaves between steps.  Rank 0's health check names it within
+    its 3 s limit, and the next step's all-gather fails with RankFailure
+    within the process group's 10 s timeout instead of waiting forever."""
+    ret = _run_failure("leave")
+    assert ret[1] == ("left",)
+    hc, st = ret[0]
+    assert hc[0] == "RankFailure" and hc[2] == 1 and hc[1] < 6.0, hc
+    assert st[0] == "RankFailure" and st[1] < 30.0, st
+
+
+def test_mismatched_split_is_refused_on_every_rank():
+    """Ranks that disagree on the total KV length stop at the first call's
+    plan check with SplitMismatch, before any partial is exchanged."""
+    ret = _run_failure("mismatch")
+    assert ret[0][0] == "SplitMismatch" and ret[1][0] == "SplitMismatch", ret
