@@ -427,24 +427,26 @@ bml_status check_decode_shape(uint32_t n_heads, uint32_t n_kv, uint32_t head_dim
 
 // Schedule knobs of the claimed-schedule kernel (decode_bulk_kernel).
 struct BulkPlan {
-    uint32_t claim_tiles = 2;  // tiles per claim
-    uint32_t join_min = 8;     // unclaimed tiles worth a join
+    uint32_t claim_tiles = 4;  // tiles per claim
+    uint32_t join_min = 4;     // unclaimed tiles per CTA on a sequence worth a join
     uint32_t merge_rows = 8;   // q-head rows per merge item
     uint32_t merge_wpr = 1;    // warps sharing one row in the merge
     uint32_t merge_dsplit = 1; // head-dim slices per merge item
 };
 
-// Tiles per claim: two (~2.6 us of one SM at the HBM rate; measured on
-// B200: with one tile a claim's atomic, issued one claim ahead, no longer
-// hides behind the ring and the Llama-3 batch streams at 6.0 instead of 7.3
-// TB/s).  A started sequence is joined only while it has at least 4 claims
-// left: a join costs three dependent round trips (~3 us).
+// Tiles per claim: four (~5 us of one SM at the HBM rate).  Measured on
+// B200: with one tile per claim a claim's atomic, issued one claim ahead, no
+// longer hides behind the ring (the Llama-3 batch streams at 6.0 instead of
+// 7.3 TB/s); four beat two by 2-12% on the Llama-3 and ragged TinyLlama
+// batches, and claiming a sequence's last 4-16 tiles one at a time, to even
+// out the end, lost 1-11% to the same atomic latency.  A started sequence is
+// joined only while it has at least 4 unclaimed tiles per CTA on it: a join
+// costs three dependent round trips (~3 us), about two tiles.
 // Merge: a row of a sequence has about nph * (grid / n_seqs + 2) partial
 // slots; each warp combines up to 16 of them in one round of loads, so a
 // row is shared by up to 8 warps (one long sequence: one row per CTA), and
 // where one warp per row suffices and the items would not fit one round of
-// the grid, a warp takes two rows.  join_min: a started sequence is joined
-// only while it has at least 4 claims left.
+// the grid, a warp takes two rows.
 BulkPlan bulk_plan(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, uint32_t nph, uint32_t parts_per_seq,
                    int grid) {
     BulkPlan b;

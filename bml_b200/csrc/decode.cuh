@@ -37,7 +37,7 @@ struct DecodeParams {
     float *part_o;         // [n_seqs][n_heads][D]
     float *slot_ml;        // scratch [n_slots][n_heads][2]
     float *slot_o;         // scratch [n_slots][n_heads][D]
-    uint32_t *counters;    // scratch [4][kMaxSeqsPerLaunch] words, zero between calls
+    uint32_t *counters;    // scratch [5][kMaxSeqsPerLaunch] words, zero between calls
     uint32_t *err;         // scratch error word
     uint32_t n_seqs, n_heads, n_kv;
     uint32_t rows_per_tile;   // T
@@ -54,7 +54,7 @@ struct DecodeParams {
     uint32_t *part_tiles;     // [n_seqs * parts_per_seq] tiles in each part (0: empty); zero between calls
     uint32_t parts_per_seq;   // parts a sequence may have (>= 1)
     uint32_t claim_tiles;     // tiles per claim
-    uint32_t join_min;        // unclaimed tiles that make a started sequence worth joining
+    uint32_t join_min;        // unclaimed tiles per CTA on a started sequence that make it worth joining
     uint32_t merge_rows;      // q-head rows per merge item (1, 2, 4, 8 or 16)
     uint32_t merge_wpr;       // consumer warps sharing one row in the merge (1, 2, 4 or 8)
     uint32_t merge_dsplit;    // head-dim slices of a row block, one merge item each (1, 2 or 4)

@@ -95,6 +95,8 @@ __host__ __device__ __forceinline__ uint32_t ktile_bytes_of(uint32_t T, uint32_t
 
 template <int D, int G>
 uint32_t smem_bytes(uint32_t T, uint32_t row_bytes) {
+    // the merge stages its slots in the ring: 8 warps' batches fit in it
+    static_assert(kWarps * 32u * (D + 3u) * 4u <= kStages * 2u * 32768u, "merge staging exceeds the ring");
     return kStages * 2u * ktile_bytes_of(T, row_bytes) + BCfg<D, G>::SCR + BCfg<D, G>::MERGE + 128u;
 }
 
@@ -176,19 +178,38 @@ __device__ __noinline__ bool claim_item(const DecodeParams &p, const unsigned lo
     return true;
 }
 
+template <int BYTES>
+__device__ __forceinline__ void cp_async(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(smem_u32(dst)), "l"(src), "n"(BYTES)
+                 : "memory");
+}
+
+// Shared-memory bytes one consumer warp stages per batch of merge slots.
+template <int D>
+__host__ __device__ constexpr uint32_t merge_stage_bytes() {
+    return 32u * (D + 3u) * 4u;
+}
+
 // This warp's share of the partial slots of RW q-head rows (qh[i]) of
 // sequence sq, for VS head dims per lane starting at dim0: slots j = sub,
-// sub + wpr, ... of the nsub = parts * nph slots, UN of them in flight per
-// lane (within the 168 registers of a 9-warp CTA), combined with the
-// log-sum-exp rule into (M, L, O) relative to M.  Empty parts (0 tiles) and
+// sub + wpr, ... of the nsub = parts * nph slots, combined with the
+// log-sum-exp rule into (M, L, O) relative to M.  A batch of up to 32 / RW
+// slots per row is staged in the warp's shared memory with cp.async first
+// (lane u also copies slot u's (m, l) and tile count), so all of its loads
+// are in flight at once and take no registers.  Empty parts (0 tiles) and
 // slots of warps that saw no valid row (m = -inf) are skipped by selection,
 // never multiplied (their bytes may be stale).
 template <int D, int VS, int RW>
 __device__ __forceinline__ void merge_share(const DecodeParams &p, uint32_t sq, const uint32_t (&qh)[RW],
                                             uint32_t dim0, uint32_t nsub, uint32_t nph, uint32_t sub, uint32_t wpr,
-                                            int lane, float (&M)[RW], float (&L)[RW], float (&O)[RW][VS]) {
-    constexpr int UN = (VS == 4 ? 8 : VS == 2 ? 16 : 24) / RW;
+                                            int lane, uint8_t *wstage, float (&M)[RW], float (&L)[RW],
+                                            float (&O)[RW][VS]) {
+    constexpr int UN = 32 / RW;
     constexpr float NEG_INF = -INFINITY;
+    // staging: o [RW][UN][32 * VS] | (m, l) [RW][UN] | tiles [RW][UN]
+    float *so = reinterpret_cast<float *>(wstage);
+    float2 *sml = reinterpret_cast<float2 *>(so + RW * UN * 32 * VS);
+    uint32_t *stl = reinterpret_cast<uint32_t *>(sml + RW * UN);
 #pragma unroll
     for (int i = 0; i < RW; ++i) {
         M[i] = NEG_INF;
@@ -197,47 +218,42 @@ __device__ __forceinline__ void merge_share(const DecodeParams &p, uint32_t sq, 
         for (int e = 0; e < VS; ++e) O[i][e] = 0.f;
     }
     for (uint32_t j0 = sub; j0 < nsub; j0 += (uint32_t)UN * wpr) {
-        uint32_t tl[RW][UN];
-        float2 ml[RW][UN];
-        float ov[RW][UN][VS];
+        const uint32_t nb = min((uint32_t)UN, (nsub - j0 + wpr - 1) / wpr);  // slots of this batch
 #pragma unroll
         for (int i = 0; i < RW; ++i) {
-#pragma unroll
-            for (int u = 0; u < UN; ++u) {
-                const uint32_t jj = j0 + (uint32_t)u * wpr;
-                tl[i][u] = 0u;
-                if (jj < nsub) {
-                    const uint32_t prt = sq * p.parts_per_seq + jj / nph;
-                    const size_t srow = ((size_t)prt * nph + jj % nph) * p.n_heads + qh[i];
-                    tl[i][u] = __ldcg(&p.part_tiles[prt]);
-                    ml[i][u] = __ldcg(reinterpret_cast<const float2 *>(p.slot_ml + srow * 2));
-                    const float *src = p.slot_o + srow * D + dim0 + lane * VS;
-                    if constexpr (VS == 4) {
-                        const float4 x = __ldcg(reinterpret_cast<const float4 *>(src));
-                        ov[i][u][0] = x.x, ov[i][u][1] = x.y, ov[i][u][2] = x.z, ov[i][u][3] = x.w;
-                    } else if constexpr (VS == 2) {
-                        const float2 x = __ldcg(reinterpret_cast<const float2 *>(src));
-                        ov[i][u][0] = x.x, ov[i][u][1] = x.y;
-                    } else {
-                        ov[i][u][0] = __ldcg(src);
-                    }
-                }
+            for (uint32_t u = 0; u < nb; ++u) {
+                const uint32_t jj = j0 + u * wpr;
+                const uint32_t prt = sq * p.parts_per_seq + jj / nph;
+                const size_t srow = ((size_t)prt * nph + jj % nph) * p.n_heads + qh[i];
+                cp_async<VS * 4>(so + ((size_t)i * UN + u) * 32 * VS + lane * VS,
+                                 p.slot_o + srow * D + dim0 + lane * VS);
+            }
+            if ((uint32_t)lane < nb) {
+                const uint32_t jj = j0 + (uint32_t)lane * wpr;
+                const uint32_t prt = sq * p.parts_per_seq + jj / nph;
+                const size_t srow = ((size_t)prt * nph + jj % nph) * p.n_heads + qh[i];
+                cp_async<8>(sml + i * UN + lane, p.slot_ml + srow * 2);
+                cp_async<4>(stl + i * UN + lane, p.part_tiles + prt);
             }
         }
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        __syncwarp();  // every lane's copies are visible to the whole warp
 #pragma unroll
         for (int i = 0; i < RW; ++i) {
-#pragma unroll
-            for (int u = 0; u < UN; ++u) {
-                if (tl[i][u] == 0u || ml[i][u].x == NEG_INF) continue;
-                const float Mn = fmaxf(M[i], ml[i][u].x);
+            for (uint32_t u = 0; u < nb; ++u) {
+                const float2 ml = sml[i * UN + u];
+                if (stl[i * UN + u] == 0u || ml.x == NEG_INF) continue;
+                const float Mn = fmaxf(M[i], ml.x);
                 const float a = M[i] == NEG_INF ? 0.f : fast_exp2(M[i] - Mn);
-                const float b = fast_exp2(ml[i][u].x - Mn) * ml[i][u].y;
+                const float b = fast_exp2(ml.x - Mn) * ml.y;
                 L[i] = L[i] * a + b;
+                const float *ov = so + ((size_t)i * UN + u) * 32 * VS + lane * VS;
 #pragma unroll
-                for (int e = 0; e < VS; ++e) O[i][e] = O[i][e] * a + ov[i][u][e] * b;
+                for (int e = 0; e < VS; ++e) O[i][e] = O[i][e] * a + ov[e] * b;
                 M[i] = Mn;
             }
         }
+        __syncwarp();  // the batch is read before the next one lands
     }
 }
 
@@ -261,19 +277,21 @@ __device__ __forceinline__ void merge_store(const DecodeParams &p, size_t row, u
 // (warp w takes row w / wpr and the slots w % wpr (mod wpr); their running
 // (M, L, O) are combined in warp order through shared memory), or, with RW
 // = 2, each warp takes two rows.  Every consumer thread calls it (the
-// combine has a named barrier).  Not inlined: its load buffers then take no
-// registers from the streaming loop.
+// combine has a named barrier).  `stage` is the ring's shared memory, idle
+// once the stream has ended.  Not inlined, so that it takes no registers
+// from the streaming loop.
 template <int D, int VS, int RW>
 __device__ __noinline__ void merge_item(const DecodeParams &p, uint32_t sq, uint32_t row0, uint32_t dim0,
                                            uint32_t nsub, uint32_t nph, uint32_t wpr, int warp, int lane,
-                                           float *mscr) {
+                                           float *mscr, uint8_t *stage) {
     constexpr float NEG_INF = -INFINITY;
     const uint32_t sub = (uint32_t)warp % wpr;
     uint32_t qh[RW];
 #pragma unroll
     for (int i = 0; i < RW; ++i) qh[i] = RW == 2 ? row0 + (uint32_t)warp * 2u + i : row0 + (uint32_t)warp / wpr;
     float M[RW], L[RW], O[RW][VS];
-    merge_share<D, VS, RW>(p, sq, qh, dim0, nsub, nph, RW == 2 ? 0u : sub, RW == 2 ? 1u : wpr, lane, M, L, O);
+    merge_share<D, VS, RW>(p, sq, qh, dim0, nsub, nph, RW == 2 ? 0u : sub, RW == 2 ? 1u : wpr, lane,
+                           stage + (size_t)warp * merge_stage_bytes<D>(), M, L, O);
     if (RW == 1 && wpr > 1) {
         float *mine = mscr + warp * (D + 4);
         if (lane == 0) {
@@ -344,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
     uint32_t *const claim_c = p.counters;
     unsigned long long *const state = reinterpret_cast<unsigned long long *>(p.counters + kMaxSeqsPerLaunch);
     uint32_t *const queue = p.counters + 3 * kMaxSeqsPerLaunch;  // completed sequences + 1, in order
+    uint32_t *const left_c = p.counters + 4 * kMaxSeqsPerLaunch;  // visits that ended
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t nph = kWarps / p.n_kv;  // warps per kv head = partial slots per part
@@ -400,41 +419,46 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
             np = __shfl_sync(kFull, np, 0);
             post_ctl(kEnd, item, np, seq);
         };
-        // Warp: the sequence with the most unclaimed tiles among those worth
-        // joining (lowest index on ties), kNone if there is none.  Worth
-        // joining: a part is left, and no CTA is on it yet, or it has at
-        // least join_min unclaimed tiles (a smaller remainder is finished
-        // sooner by the CTAs already on it than a join takes).  A sequence
-        // with unclaimed tiles has every CTA that took a part of it still on
-        // it, so the rule leaves no tile behind.  The counters only grow, so a
+        // Warp: the sequence where a joining CTA helps most -- the most
+        // unclaimed tiles per CTA already on it (reserved parts minus ended
+        // visits), lowest index on ties -- among those with a part left and,
+        // unless no CTA is on it yet, at least join_min unclaimed tiles per
+        // CTA on it (a smaller remainder is finished by those CTAs sooner
+        // than a join takes); kNone if there is none.  A sequence with
+        // unclaimed tiles has every CTA that took a part of it still on it,
+        // so the rule leaves no tile behind.  The counters only grow, so a
         // stale read never hides remaining work.
         auto pick = [&]() -> uint32_t {
-            uint32_t cl[kMaxSeqsPerLaunch / 32], rs[kMaxSeqsPerLaunch / 32];
+            uint32_t cl[kMaxSeqsPerLaunch / 32], rs[kMaxSeqsPerLaunch / 32], lf[kMaxSeqsPerLaunch / 32];
 #pragma unroll
             for (int i = 0; i < kMaxSeqsPerLaunch / 32; ++i) {
                 const uint32_t s = (uint32_t)i * 32u + (uint32_t)lane;
-                cl[i] = rs[i] = 0u;
+                cl[i] = rs[i] = lf[i] = 0u;
                 if (s < p.n_seqs) {
                     cl[i] = ld_relaxed_gpu(&claim_c[s]);
                     rs[i] = (uint32_t)(ld_relaxed_gpu_u64(&state[s]) >> 32);
+                    lf[i] = ld_relaxed_gpu(&left_c[s]);
                 }
             }
-            uint32_t best = kNone, best_rem = 0;
+            uint32_t best = kNone, best_score = 0;
 #pragma unroll
             for (int i = 0; i < kMaxSeqsPerLaunch / 32; ++i) {
                 if ((uint32_t)i * 32u >= p.n_seqs) break;
                 const uint32_t s = (uint32_t)i * 32u + (uint32_t)lane;
-                uint32_t rem = 0;
+                uint32_t score = 0;  // unclaimed tiles per CTA on it, scaled by 16; 0 = not worth joining
                 if (s < p.n_seqs) {
                     const uint32_t nt = tiles_of(p, s), h = homes_of(p, s);
-                    const uint32_t claimed = h + cl[i];
-                    rem = (claimed < nt && h + rs[i] < p.parts_per_seq) ? nt - claimed : 0u;
-                    if (rem < p.join_min && (h > 0 || rs[i] > 0)) rem = 0u;
+                    const uint32_t claimed = h + cl[i], taken = h + rs[i];
+                    if (claimed < nt && taken < p.parts_per_seq) {
+                        const uint32_t rem = nt - claimed;
+                        const uint32_t on = taken > lf[i] ? taken - lf[i] : 0u;
+                        if (on == 0 || rem >= p.join_min * on) score = (16u * rem) / (on + 1u) + 1u;
+                    }
                 }
-                const uint32_t mx = __reduce_max_sync(kFull, rem);
-                if (mx > best_rem) {
-                    best_rem = mx;
-                    best = (uint32_t)i * 32u + (uint32_t)(__ffs(__ballot_sync(kFull, rem == mx)) - 1);
+                const uint32_t mx = __reduce_max_sync(kFull, score);
+                if (mx > best_score) {
+                    best_score = mx;
+                    best = (uint32_t)i * 32u + (uint32_t)(__ffs(__ballot_sync(kFull, score == mx)) - 1);
                 }
             }
             return best;
@@ -444,6 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
         // part, current claim [c, c + cn), next tile j of it, tiles of the
         // visit so far vt, prefetched next claim pref
         uint32_t s = 0, part = 0, c = 0, cn = 0, j = 0, vt = 0, pref = 0;
+
         // Warp: opens a joining visit on the best pick and posts its visit
         // record; false if no tile is left anywhere (or on timeout).
         auto join = [&]() -> bool {
@@ -544,6 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
             }
             flush = __shfl_sync(kFull, flush, 0);
             if (flush) {
+                if (lane == 0) atomicAdd(&left_c[s], 1u);  // this CTA leaves the sequence
                 const uint32_t ss = __shfl_sync(kFull, s, 0), pp = __shfl_sync(kFull, part, 0);
                 const uint32_t tt = __shfl_sync(kFull, vt, 0);
                 if (!post_ctl(kFlush, ss, pp, tt)) break;
@@ -803,13 +829,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
             const uint32_t row0 = k / DS * R, dim0 = k % DS * (D / DS);
             const uint32_t nsub = np * nph;
             if (rw == 2)
-                merge_item<D, D / 32, 2>(p, sq, row0, 0u, nsub, nph, 1u, warp, lane, mscr);
+                merge_item<D, D / 32, 2>(p, sq, row0, 0u, nsub, nph, 1u, warp, lane, mscr, stages);
             else if (DS == 1)
-                merge_item<D, D / 32, 1>(p, sq, row0, 0u, nsub, nph, wpr, warp, lane, mscr);
+                merge_item<D, D / 32, 1>(p, sq, row0, 0u, nsub, nph, wpr, warp, lane, mscr, stages);
             else if (DS == 2)
-                merge_item<D, D / 64, 1>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr);
+                merge_item<D, D / 64, 1>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr, stages);
             else if constexpr (D >= 128)
-                merge_item<D, D / 128, 1>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr);
+                merge_item<D, D / 128, 1>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr, stages);
             if (threadIdx.x == 0) {
                 uint32_t nxt = kNoItem, nseq = 0, nnp = 0;
                 if (!claim_item(p, state, queue, ips, items, flags, nxt, nseq, nnp)) nxt = kNoItem;
@@ -832,11 +858,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
     if (flags[3]) {
         __threadfence();
         // claim counters [0, 256), state words (two u32 each) after them,
-        // merge-item claims [768, 1024)
-        for (uint32_t i = threadIdx.x; i < 4u * kMaxSeqsPerLaunch; i += blockDim.x) {
+        // the completion queue [768, 1024), ended visits [1024, 1280)
+        for (uint32_t i = threadIdx.x; i < 5u * kMaxSeqsPerLaunch; i += blockDim.x) {
             const uint32_t sq = i < (uint32_t)kMaxSeqsPerLaunch        ? i
                                 : i < 3u * (uint32_t)kMaxSeqsPerLaunch ? (i - kMaxSeqsPerLaunch) / 2u
-                                                                       : i - 3u * kMaxSeqsPerLaunch;
+                                                                       : i % kMaxSeqsPerLaunch;
             if (sq < p.n_seqs) p.counters[i] = 0u;
         }
         for (uint32_t i = threadIdx.x; i < p.n_seqs * p.parts_per_seq; i += blockDim.x) p.part_tiles[i] = 0u;
