@@ -110,3 +110,16 @@ def test_weight_path_rejects_on_host(L):
     assert lib.bml_matmul_f64(18, 64, L.GGUF_F32, 4, 4, 16, 4, 16, None, 0, None) == L.BML_E_INVALID
     size = C.c_size_t()
     assert lib.bml_matmul_workspace_size(4096, C.byref(size)) == L.BML_OK and size.value == 160 * 4096 * 8
+
+
+def test_rust_binding_declares_every_product_entry_point():
+    """crates/bml-attn-cuda/src/ffi.rs (the binding a bml maintainer adds)
+    declares exactly the product entry points of bml_attn.h, bml_weights.h
+    and bml_gguf.h; the test-only bml_diag.h is left out."""
+    text = open(os.path.join(ROOT, "crates", "bml-attn-cuda", "src", "ffi.rs")).read()
+    rust = set(re.findall(r"pub fn (bml_[a-z0-9_]+)\s*\(", text))
+    product = set()
+    for h in ("bml_attn.h", "bml_weights.h", "bml_gguf.h"):
+        t = re.sub(r"/\*.*?\*/", "", open(os.path.join(ROOT, "include", h)).read(), flags=re.S)
+        product |= set(re.findall(r"\b(bml_[a-z0-9_]+)\s*\(", t))
+    assert rust == product, (sorted(product - rust), sorted(rust - product))
