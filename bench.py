@@ -616,7 +616,7 @@ def run_b200(args):
         res["batched_tinyllama"] = tiny
         res["gpu_launches"] += sub_steps
         torch.cuda.empty_cache()
-        lc = run_longctx_obj(dev, sub_steps, max(3, args.warmup), dist, peaks, cpu / 2)
+        lc = run_longctx_obj(dev, sub_steps, max(3, args.warmup), dist, peaks, cpu / 2, args.kvsplit)
         res["gpu_launches"] += sub_steps * lc.pop("launches_per_step")
         res["longctx"] = lc
     emit(res, dist)
@@ -658,7 +658,7 @@ def e2e_decode(q, batch, ws, args, dist, step_bytes):
             "steps": n, "ms_per_step": round(ms / n, 5)}
 
 
-def run_longctx_obj(dev, steps, warmup, dist, peaks, cpu_budget):
+def run_longctx_obj(dev, steps, warmup, dist, peaks, cpu_budget, kvsplit="peer"):
     """One 131072-position sequence (Llama-3-8B heads, bf16 KV) split along
     its KV length over the ranks; per-rank (m, l, o) partials exchanged and
     merged ("strong").  One GPU runs the plain decode of the whole
@@ -678,7 +678,7 @@ def run_longctx_obj(dev, steps, warmup, dist, peaks, cpu_budget):
     batch = bml_b200.SeqBatch([k], [v])
     ws = bml_b200.Workspace(dev).ensure(1, H, d)
     merged = torch.empty(1, H, d, dtype=torch.float32, device=dev)
-    step = sharding.KVSplitDecode(dist.pg, dist.world, H, d, dev)
+    step = sharding.KVSplitDecode(dist.pg, dist.world, H, d, dev, fused=kvsplit == "peer")
     fn = lambda: step(q, batch, ws, out=merged, total_len=total_len)  # noqa: E731
     fn()
     torch.cuda.synchronize()
@@ -686,10 +686,10 @@ def run_longctx_obj(dev, steps, warmup, dist, peaks, cpu_budget):
     step_bytes = decode_step_bytes(batch, H)
     total = dist.sum(step_bytes)
     gbs = total * steps / (ms * 1e-3) / 1e9
-    if dist.world > 1:
+    if dist.world > 1 and kvsplit == "nccl":
         kfn = lambda: bml_b200.decode_partial(q, batch, workspace=ws)  # noqa: E731
-    else:  # what the one-GPU step runs
-        kfn = lambda: bml_b200.decode_batched(q, batch, out=merged, workspace=ws)  # noqa: E731
+    else:  # one launch: the whole step (with the exchange inside it on several GPUs)
+        kfn = fn
     kms = kernel_ms(kfn)
     ws.check()
     ach = step_bytes / (kms * 1e-3) / 1e9
@@ -698,18 +698,22 @@ def run_longctx_obj(dev, steps, warmup, dist, peaks, cpu_budget):
            "ms_per_step": round(ms / steps, 5), "steps": steps, "scaling": "strong",
            "config": {"workload": "longctx", "context": total_len, "n_heads": H, "n_kv_heads": Hkv,
                       "head_dim": d, "kv_dtype": "bf16",
-                      "split": (f"KV length over {dist.world} GPUs, NCCL all_gather of (m, l, o) + LSE merge"
-                                if dist.world > 1 else "one GPU: the whole sequence, plain decode"),
+                      "split": ("one GPU: the whole sequence, plain decode" if dist.world == 1 else
+                                f"KV length over {dist.world} GPUs; per-(head, 32 dims) partials exchanged over "
+                                "peer memory and merged inside the decode kernel" if kvsplit == "peer" else
+                                f"KV length over {dist.world} GPUs, NCCL all_gather of (m, l, o) + LSE merge"),
                       "l2": "512 MiB of KV (K + V) per step, all ranks"},
            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
                         "frac": round(ach / hbm, 4), "frac_spec": round(ach / SPEC_PEAKS["hbm_gbs"], 4),
                         "traffic": profile_traffic("decode_longctx.txt") if dist.world == 1 else None,
                         "kernel": "decode_bulk_kernel", "kernel_ms": round(kms, 5),
                         "algorithmic_bytes_per_launch": step_bytes},
-           # per step: decode_bulk_kernel; with several ranks also
+           # per step: decode_bulk_kernel; with the NCCL exchange also
            # merge_lse_packed_kernel, with NCCL's all-gather between
-           "launches_per_step": 2 if dist.world > 1 else 1,
+           "launches_per_step": 2 if dist.world > 1 and kvsplit == "nccl" else 1,
            "clocks": clocks}
+    if dist.world > 1:
+        step.close()
     if dist.world == 1 and cpu_budget > 0:
         v, thr, desc = cpu_decode_sample("longctx", cpu_budget)
         res["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": thr, "kind": "port", "sample": desc}
@@ -717,7 +721,8 @@ def run_longctx_obj(dev, steps, warmup, dist, peaks, cpu_budget):
 
 
 def run_longctx(args, dist, peaks, res):
-    obj = run_longctx_obj(dist.device, args.steps, args.warmup, dist, peaks, 0 if args.no_cpu else args.cpu_budget)
+    obj = run_longctx_obj(dist.device, args.steps, args.warmup, dist, peaks, 0 if args.no_cpu else args.cpu_budget,
+                          args.kvsplit)
     res.update(obj)
     res["metric"] = DECODE_METRIC
     res["dtype"] = "f32 (bf16 KV)"
@@ -1133,6 +1138,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-sub", action="store_true",
                     help="default line without its batched_tinyllama and longctx objects")
+    ap.add_argument("--kvsplit", default="peer", choices=["peer", "nccl"],
+                    help="longctx over several GPUs: exchange inside the decode kernel (peer) or NCCL all-gather")
     ap.add_argument("--sub-steps", type=int, default=500,
                     help="timed steps of the batched_tinyllama and longctx objects (at least --steps)")
     ap.add_argument("--gguf-threads", type=int, default=8, help="host threads of bml_gguf_upload (gguf_load)")

@@ -117,6 +117,12 @@ SIGNATURES = {
     "bml_gguf_upload": (_st, [_vp, C.POINTER(C.c_uint64), _u32, C.POINTER(_vp), _u32]),
     "bml_attn_workspace_check": (_st, [_vp, _sz, _vp]),
     "bml_attn_noalloc_check": (_st, [_vp]),
+    "bml_kvsplit_create": (_st, [_i32, _u32, _u32, _u32, _u32, C.POINTER(_vp)]),
+    "bml_kvsplit_handle": (_st, [_vp, _vp, _sz]),
+    "bml_kvsplit_open": (_st, [_vp, _vp, _sz]),
+    "bml_attn_decode_kvsplit": (_st, [_vp, C.POINTER(bml_seq_desc), _u32, _u32, _u32, C.c_int, C.c_float, _vp,
+                                      _vp, _vp, _sz, _vp]),
+    "bml_kvsplit_destroy": (_st, [_vp]),
     # include/bml_diag.h (test-only)
     "bml_diag_exp2": (_st, [_vp, _u32, _vp, _vp]),
     "bml_diag_decode_batched": (_st, [C.POINTER(bml_seq_desc), _u32, _u32, _u32, _u32, C.c_int,
@@ -125,6 +131,7 @@ SIGNATURES = {
 
 BML_DIAG_DECODE_DEFAULT, BML_DIAG_DECODE_CUDA_CORE = 0, 1  # include/bml_diag.h
 BML_DIAG_STALL = 1
+BML_KVSPLIT_HANDLE_BYTES = 64  # include/bml_attn.h
 
 _lock = threading.Lock()
 _lib = None

@@ -480,12 +480,21 @@ uint32_t max_homes(const bml::DecodeParams &p, uint32_t total, uint32_t grid) {
     return m;
 }
 
-// Shared body of bml_attn_decode_batched / _partial (and their test-only
-// variant, whose kernel choice, wait limit and behaviour flags are given).
+// A KV split over GPUs: this rank, the call's epoch and every rank's
+// exchange buffer (mapped into this process).
+struct ExchangeArgs {
+    uint32_t world = 1, rank = 0, epoch = 0;
+    float *base[bml::kMaxExchangeRanks] = {};
+};
+
+// Shared body of bml_attn_decode_batched / _partial, the test-only variant
+// (kernel choice, wait limit and behaviour flags given) and the KV split
+// over GPUs (exchange given).
 bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv,
                        uint32_t head_dim, bml_dtype dt, float scale, const float *q, float *out, float *pm,
                        float *pl, float *po, void *workspace, size_t ws_bytes, void *stream, int mode,
-                       const char *fn, int force_kernel = 0, uint64_t wait_ns = bml::kWaitNs, uint32_t diag = 0) {
+                       const char *fn, int force_kernel = 0, uint64_t wait_ns = bml::kWaitNs, uint32_t diag = 0,
+                       const ExchangeArgs *xa = nullptr) {
     bml_status st = check_decode_shape(n_heads, n_kv, head_dim, dt, fn);
     if (st != BML_OK) return st;
     if (!seqs || n_seqs == 0) return fail(BML_E_INVALID, "%s: no sequences", fn);
@@ -513,6 +522,9 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
     const uint32_t group = n_heads / n_kv;
     const bml::DecodeKernel kern =
         force_kernel == BML_DIAG_DECODE_CUDA_CORE ? bml::kKernCuda : bml::decode_select(dt, head_dim, n_kv, group);
+    const bool split = xa && xa->world > 1;
+    if (split && (kern != bml::kKernBulk || n_seqs != 1 || mode != bml::kModeFinal))
+        return fail(BML_E_UNSUPPORTED, "%s: the KV split over GPUs takes one 16-bit sequence", fn);
     static thread_local bml::DecodeParams p;  // ~8 KB, kept off the stack
     for (uint32_t base = 0; base < n_seqs; base += (uint32_t)bml::kMaxSeqsPerLaunch) {
         const uint32_t ns = std::min<uint32_t>(n_seqs - base, (uint32_t)bml::kMaxSeqsPerLaunch);
@@ -554,6 +566,16 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
             p.merge_rows = plan.merge_rows;
             p.merge_wpr = plan.merge_wpr;
             p.merge_dsplit = plan.merge_dsplit;
+            if (split) {  // one merge item per exchange unit: a row x 32 dims
+                p.merge_rows = 1;
+                p.merge_wpr = 8;
+                p.merge_dsplit = head_dim / 32;
+                p.x_world = xa->world;
+                p.x_rank = xa->rank;
+                p.x_epoch = xa->epoch;
+                p.x_units = n_heads * (head_dim / 32);
+                for (uint32_t r = 0; r < xa->world; ++r) p.x_base[r] = xa->base[r];
+            }
             p.sched = ws.sched;
             p.part_tiles = ws.part_tiles;
         } else {
@@ -898,6 +920,121 @@ BML_API bml_status bml_attn_noalloc_check(void *stream) {
     bml_status st = noalloc_scratch(current_device(), &scratch);
     if (st != BML_OK) return st;
     return bml_attn_workspace_check(scratch, kNoAllocScratchBytes, stream);
+}
+
+// ---------------------------------------------------------------------------
+// KV split of one sequence over GPUs with the exchange in the decode kernel
+// ---------------------------------------------------------------------------
+struct bml_kvsplit {
+    int32_t device = 0;
+    uint32_t rank = 0, world = 1, n_heads = 0, head_dim = 0, units = 0, epoch = 0;
+    float *buf = nullptr;  // this rank's exchange buffer
+    size_t bytes = 0;
+    float *peer[bml::kMaxExchangeRanks] = {};  // every rank's buffer, mapped here
+    bool opened = false;
+};
+
+BML_API bml_status bml_kvsplit_create(int32_t device, uint32_t rank, uint32_t world, uint32_t n_heads,
+                                      uint32_t head_dim, bml_kvsplit **out) {
+    const char *fn = "bml_kvsplit_create";
+    if (!out) return fail(BML_E_INVALID, "%s: null output", fn);
+    *out = nullptr;
+    if (world == 0 || world > (uint32_t)bml::kMaxExchangeRanks || rank >= world)
+        return fail(BML_E_INVALID, "%s: rank %u of world %u (at most %d ranks)", fn, rank, world,
+                    bml::kMaxExchangeRanks);
+    if (n_heads == 0 || n_heads > 256 || !(head_dim == 64 || head_dim == 128))
+        return fail(BML_E_UNSUPPORTED, "%s: %u heads of dim %u", fn, n_heads, head_dim);
+    DeviceGuard g(device);
+    bml_kvsplit *h = new bml_kvsplit();
+    h->device = device;
+    h->rank = rank;
+    h->world = world;
+    h->n_heads = n_heads;
+    h->head_dim = head_dim;
+    h->units = n_heads * (head_dim / 32);
+    h->bytes = bml::exchange_bytes(h->units);
+    cudaError_t e = cudaMalloc(&h->buf, h->bytes);
+    if (e == cudaSuccess) e = cudaMemset(h->buf, 0, h->bytes);  // flags start below every epoch
+    if (e != cudaSuccess) {
+        if (h->buf) cudaFree(h->buf);
+        delete h;
+        return cuda_fail(e, fn);
+    }
+    h->peer[rank] = h->buf;
+    *out = h;
+    return ok();
+}
+
+BML_API bml_status bml_kvsplit_handle(const bml_kvsplit *h, void *handle_out, size_t bytes) {
+    if (!h || !handle_out || bytes < BML_KVSPLIT_HANDLE_BYTES)
+        return fail(BML_E_INVALID, "bml_kvsplit_handle: null argument or %zu < %d bytes", bytes,
+                    BML_KVSPLIT_HANDLE_BYTES);
+    DeviceGuard g(h->device);
+    cudaIpcMemHandle_t m;
+    CUDA_TRY(cudaIpcGetMemHandle(&m, h->buf), "bml_kvsplit_handle");
+    memcpy(handle_out, &m, sizeof m);
+    return ok();
+}
+
+BML_API bml_status bml_kvsplit_open(bml_kvsplit *h, const void *handles, size_t bytes) {
+    const char *fn = "bml_kvsplit_open";
+    if (!h || !handles) return fail(BML_E_INVALID, "%s: null argument", fn);
+    if (h->opened) return fail(BML_E_INVALID, "%s: already open", fn);
+    if (bytes != (size_t)h->world * BML_KVSPLIT_HANDLE_BYTES)
+        return fail(BML_E_INVALID, "%s: %zu bytes of handles for %u ranks", fn, bytes, h->world);
+    DeviceGuard g(h->device);
+    for (uint32_t r = 0; r < h->world; ++r) {
+        if (r == h->rank) continue;
+        cudaIpcMemHandle_t m;
+        memcpy(&m, static_cast<const char *>(handles) + (size_t)r * BML_KVSPLIT_HANDLE_BYTES, sizeof m);
+        void *ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, m, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (uint32_t q = 0; q < r; ++q)
+                if (q != h->rank && h->peer[q]) cudaIpcCloseMemHandle(h->peer[q]);
+            return cuda_fail(e, fn);
+        }
+        h->peer[r] = static_cast<float *>(ptr);
+    }
+    h->opened = true;
+    return ok();
+}
+
+BML_API bml_status bml_attn_decode_kvsplit(bml_kvsplit *h, const bml_seq_desc *slice_host, uint32_t n_heads,
+                                           uint32_t n_kv_heads, uint32_t head_dim, bml_dtype kv_dtype, float scale,
+                                           const float *q_dev, float *out_dev, void *workspace,
+                                           size_t workspace_bytes, void *stream) {
+    const char *fn = "bml_attn_decode_kvsplit";
+    if (!h || !slice_host) return fail(BML_E_INVALID, "%s: null argument", fn);
+    if (h->world > 1 && !h->opened) return fail(BML_E_INVALID, "%s: peers not opened", fn);
+    if (n_heads != h->n_heads || head_dim != h->head_dim)
+        return fail(BML_E_INVALID, "%s: %u heads of dim %u, the handle has %u of dim %u", fn, n_heads, head_dim,
+                    h->n_heads, h->head_dim);
+    DeviceGuard g(h->device);
+    if (h->world == 1)
+        return decode_impl(slice_host, 1, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev, nullptr,
+                           nullptr, nullptr, workspace, workspace_bytes, stream, bml::kModeFinal, fn);
+    ExchangeArgs xa;
+    xa.world = h->world;
+    xa.rank = h->rank;
+    if (++h->epoch == 0) h->epoch = 1;  // flags start at 0: an epoch is never 0
+    xa.epoch = h->epoch;
+    for (uint32_t r = 0; r < h->world; ++r) xa.base[r] = h->peer[r];
+    bml_status st = decode_impl(slice_host, 1, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev,
+                                nullptr, nullptr, nullptr, workspace, workspace_bytes, stream, bml::kModeFinal, fn,
+                                0, bml::kWaitNs, 0, &xa);
+    if (st != BML_OK) --h->epoch;  // nothing was launched
+    return st;
+}
+
+BML_API bml_status bml_kvsplit_destroy(bml_kvsplit *h) {
+    if (!h) return ok();
+    DeviceGuard g(h->device);
+    for (uint32_t r = 0; r < h->world; ++r)
+        if (r != h->rank && h->peer[r]) cudaIpcCloseMemHandle(h->peer[r]);
+    if (h->buf) cudaFree(h->buf);
+    delete h;
+    return ok();
 }
 
 // ---------------------------------------------------------------------------

@@ -23,6 +23,18 @@ struct DecodeSeq {
 
 constexpr int kMaxSeqsPerLaunch = 256;
 
+// KV split over GPUs: at most 8 ranks; a unit is (M, L, 2 spare, 32 dims)
+constexpr int kMaxExchangeRanks = 8;
+constexpr int kExchangeUnitFloats = 36;
+// Exchange buffer of a rank: data [2 call parities][kMaxExchangeRanks][units]
+// units of kExchangeUnitFloats, then flags [2][kMaxExchangeRanks][units] u32.
+__host__ __device__ inline size_t exchange_data_floats(uint32_t units) {
+    return 2ull * kMaxExchangeRanks * units * kExchangeUnitFloats;
+}
+inline size_t exchange_bytes(uint32_t units) {
+    return exchange_data_floats(units) * 4 + 2ull * kMaxExchangeRanks * units * 4;
+}
+
 enum DecodeMode : int { kModeFinal = 0, kModePartial = 1 };
 
 // Test-only behaviour of decode_bulk_kernel (bml_diag_decode_batched): the
@@ -60,6 +72,12 @@ struct DecodeParams {
     uint32_t merge_dsplit;    // head-dim slices of a row block, one merge item each (1, 2 or 4)
     uint32_t diag;            // kDiag* flags, 0 outside tests
     uint64_t wait_ns;         // limit of every bounded wait
+    // KV split over GPUs (x_world > 1; one sequence a launch): each merge
+    // item is one exchange unit (q-head row, 32 head dims); its rank's (M, L,
+    // O / L) goes to every rank's exchange buffer over peer memory, and the
+    // output is merged from all ranks' units in rank order
+    uint32_t x_world, x_rank, x_epoch, x_units;
+    float *x_base[kMaxExchangeRanks];  // every rank's exchange buffer, mapped here
     DecodeSeq seqs[kMaxSeqsPerLaunch];
 };
 

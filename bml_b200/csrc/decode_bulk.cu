@@ -272,6 +272,76 @@ __device__ __forceinline__ void merge_store(const DecodeParams &p, size_t row, u
     }
 }
 
+__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One warp, one exchange unit (q-head row qh, dims [dim0, dim0 + 32)) of a
+// KV split over GPUs.  This rank's (M, L, O / L) -- lane l holds dim l --
+// goes to every rank's buffer slot [parity][this rank][unit] with plain
+// stores over peer memory, then a release store of the call's epoch into
+// that rank's flag for it.  Lane r waits (bounded by p.wait_ns) for rank
+// r's flag in this rank's buffer; the ranks' units are then merged in rank
+// order (so all ranks write bit-identical outputs).  A slot is reused two
+// calls later: by then every rank has finished the call that read it (a
+// rank's next call starts after its previous one, on one stream).
+__device__ __noinline__ void exchange_store(const DecodeParams &p, uint32_t unit, uint32_t qh, uint32_t dim0,
+                                            float M, float L, float O, int lane) {
+    constexpr float NEG_INF = -INFINITY;
+    const uint32_t par = p.x_epoch & 1u, W = p.x_world;
+    const size_t data = exchange_data_floats(p.x_units);
+    const size_t mine = ((size_t)(par * kMaxExchangeRanks + p.x_rank) * p.x_units + unit) * kExchangeUnitFloats;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    for (uint32_t r = 0; r < W; ++r) {
+        float *dst = p.x_base[r] + mine;
+        if (lane == 0) {
+            dst[0] = M;
+            dst[1] = L;
+        }
+        dst[4 + lane] = O * inv;
+    }
+    __threadfence_system();  // the unit reaches every rank before its flag
+    __syncwarp();
+    const size_t fl = (size_t)(par * kMaxExchangeRanks + p.x_rank) * p.x_units + unit;
+    if ((uint32_t)lane < W) st_release_sys(reinterpret_cast<uint32_t *>(p.x_base[lane] + data) + fl, p.x_epoch);
+    bool ok = true;
+    if ((uint32_t)lane < W) {
+        const uint32_t *flag = reinterpret_cast<const uint32_t *>(p.x_base[p.x_rank] + data) +
+                               (size_t)(par * kMaxExchangeRanks + lane) * p.x_units + unit;
+        uint64_t t0 = 0;
+        for (uint32_t polls = 0; ld_acquire_sys(flag) != p.x_epoch; ++polls) {
+            const uint64_t now = globaltimer_ns();
+            if (!t0) t0 = now;
+            if (now - t0 > p.wait_ns) {
+                atomicOr(p.err, kErrTimeout);
+                ok = false;
+                break;
+            }
+            if (polls > 8) __nanosleep(32);
+        }
+    }
+    if (!__all_sync(0xffffffffu, ok)) return;  // the error word reports it
+    const float *base = p.x_base[p.x_rank];
+    float Mt = NEG_INF;
+    for (uint32_t r = 0; r < W; ++r)
+        Mt = fmaxf(Mt, __ldcv(base + ((size_t)(par * kMaxExchangeRanks + r) * p.x_units + unit) * kExchangeUnitFloats));
+    float Lt = 0.f, Ot = 0.f;
+    for (uint32_t r = 0; r < W; ++r) {
+        const float *u = base + ((size_t)(par * kMaxExchangeRanks + r) * p.x_units + unit) * kExchangeUnitFloats;
+        const float mr = __ldcv(u);
+        const float w = mr == NEG_INF ? 0.f : fast_exp2(mr - Mt) * __ldcv(u + 1);
+        Lt += w;
+        Ot += __ldcv(u + 4 + lane) * w;
+    }
+    p.out[(size_t)qh * 32u * (p.x_units / p.n_heads) + dim0 + lane] = Lt > 0.f ? Ot / Lt : 0.f;
+}
+
 // The consumer warps' merge of one item: R q-head rows starting at row0 of
 // sequence sq, head dims [dim0, dim0 + 32 * VS).  wpr warps share a row
 // (warp w takes row w / wpr and the slots w % wpr (mod wpr); their running
@@ -317,7 +387,9 @@ __device__ __noinline__ void merge_item(const DecodeParams &p, uint32_t sq, uint
             M[0] = Mt;
         }
     }
-    if (RW == 2 || sub == 0) {
+    if (RW == 1 && VS == 1 && p.x_world > 1) {
+        if (sub == 0) exchange_store(p, qh[0] * (D / 32) + dim0 / 32, qh[0], dim0, M[0], L[0], O[0][0], lane);
+    } else if (RW == 2 || sub == 0) {
 #pragma unroll
         for (int i = 0; i < RW; ++i)
             merge_store<D, VS>(p, (size_t)sq * p.n_heads + qh[i], dim0, M[i], L[i], O[i], lane);
@@ -940,6 +1012,11 @@ cudaError_t launch_decode_bulk(const DecodeParams &p, bml_dtype dt, uint32_t hea
                                                             (wpr == 1 && R == 2u * kWarps)) ||
         p.n_heads % R != 0 || !(DS == 1 || DS == 2 || DS == 4) || 32u * DS > head_dim ||
         (DS > 1 && R * wpr != (uint32_t)kWarps))
+        return cudaErrorInvalidValue;
+    // a KV split over GPUs: one sequence, items of one row x 32 dims
+    if (p.x_world > 1 && (p.x_world > (uint32_t)kMaxExchangeRanks || p.x_rank >= p.x_world || p.n_seqs != 1 ||
+                          p.mode != kModeFinal || DS * 32u != head_dim || wpr != (uint32_t)kWarps || R != 1 ||
+                          p.x_units != p.n_heads * DS || p.x_epoch == 0))
         return cudaErrorInvalidValue;
     // every home CTA's static part fits the parts of its sequence
     for (uint32_t s = 0; s < p.n_seqs; ++s) {

@@ -7,10 +7,13 @@ attention runs in one thread of one process):
   longest-processing-time first (work ~ cached length) and each GPU runs
   its own batch.  No collective.
 * Long-context decode: one sequence's KV length is cut into contiguous
-  ranges, one per GPU.  Each GPU computes the (m, l, o) partial of its
-  range (bml_attn_decode_partial), the packed partials are all-gathered
-  over NCCL (NVLink), and every GPU merges them in rank order
-  (bml_attn_merge_lse_packed), so all ranks hold bit-identical outputs.
+  ranges, one per GPU.  By default (fused) each GPU decodes its range and,
+  inside the same kernel, exchanges its per-(q head, 32 dims) partials with
+  every other GPU over peer memory and merges them in rank order
+  (bml_attn_decode_kvsplit).  The other form computes each range's (m, l, o)
+  partial (bml_attn_decode_partial), all-gathers the packed partials over
+  NCCL and merges them (bml_attn_merge_lse_packed).  Either way all ranks
+  hold bit-identical outputs.
 """
 from __future__ import annotations
 
@@ -90,7 +93,7 @@ class KVSplitDecode:
 
     def __init__(self, pg, world: int, n_heads: int, head_dim: int, device,
                  partial_fn: Callable | None = None, merge_fn: Callable | None = None,
-                 store=None, health_timeout_s: float = 10.0):
+                 store=None, health_timeout_s: float = 10.0, fused: bool = True):
         import torch
         self.pg, self.world, self.n_heads, self.d = pg, world, n_heads, head_dim
         self.device = device
@@ -105,6 +108,44 @@ class KVSplitDecode:
         self._packed = None
         self._gathered = None
         self._torch = torch
+        # the exchange inside the decode kernel: CUDA library, several ranks
+        self.fused = fused and world > 1 and partial_fn is None and merge_fn is None
+        self._peer = None
+
+    def _open_peer(self):
+        """Creates this rank's exchange buffer and maps every rank's
+        (handles all-gathered through the process group)."""
+        import ctypes as C
+
+        from . import _lib as L
+        h = C.c_void_p()
+        dev = self._torch.device(self.device).index or 0
+        L.call("bml_kvsplit_create", dev, self.rank, self.world, self.n_heads, self.d, C.byref(h))
+        buf = (C.c_char * L.BML_KVSPLIT_HANDLE_BYTES)()
+        try:
+            L.call("bml_kvsplit_handle", h, buf, L.BML_KVSPLIT_HANDLE_BYTES)
+            mine = bytes(buf)
+            every = [None] * self.world
+            self._collective("exchange-handle all-gather", self.pg.all_gather_object, every, mine)
+            blob = b"".join(every)
+            L.call("bml_kvsplit_open", h, blob, len(blob))
+        except Exception:
+            L.call("bml_kvsplit_destroy", h)
+            raise
+        self._peer = h
+
+    def close(self) -> None:
+        """Unmaps the peers' exchange buffers and frees this rank's."""
+        if self._peer is not None:
+            from . import _lib as L
+            L.call("bml_kvsplit_destroy", self._peer)
+            self._peer = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def _buffers(self, n_rows: int):
         torch = self._torch
@@ -171,6 +212,25 @@ class KVSplitDecode:
             if pending:
                 time.sleep(0.01)
 
+    def _fused_step(self, q, batch, workspace, out):
+        import ctypes as C
+
+        from . import _lib as L
+        from .attention import _need, _ptr, _stream, default_workspace, dtype_code
+        torch = self._torch
+        if self._peer is None:
+            self._open_peer()
+        _need(q, "q", torch.float32, 3)
+        if q.shape[0] != 1 or len(batch) != 1:
+            raise ValueError("the fused KV split takes one sequence")
+        if out is None:
+            out = torch.empty_like(q)
+        ws = (workspace or default_workspace(q.device.index)).ensure(1, self.n_heads, self.d)
+        L.call("bml_attn_decode_kvsplit", self._peer, batch.descs, self.n_heads, batch.n_kv, self.d,
+               dtype_code(batch.dtype), C.c_float(-1.0), _ptr(q), _ptr(out), ws.ptr, ws.nbytes, _stream(None))
+        self.steps += 1
+        return out
+
     def __call__(self, q, batch, workspace=None, out=None, total_len: int | None = None):
         torch = self._torch
         if self.world == 1 and self.partial_fn is None and self.merge_fn is None:
@@ -180,6 +240,8 @@ class KVSplitDecode:
             return decode_batched(q, batch, out=out, workspace=workspace)
         if not self._plan_checked:
             self.check_plan(total_len if total_len is not None else -1)
+        if self.fused:
+            return self._fused_step(q, batch, workspace, out)
         n_seqs = q.shape[0]
         n_rows = n_seqs * self.n_heads
         packed, gathered = self._buffers(n_rows)

@@ -18,6 +18,8 @@ pub const BML_E_UNSUPPORTED: bml_status = 6;
 }
 #[repr(C)] pub struct bml_seq_desc { pub k_dev: *const c_void, pub v_dev: *const c_void, pub len: u32, pub reserved: u32 }
 #[repr(C)] pub struct bml_gguf { _p: [u8; 0] }
+#[repr(C)] pub struct bml_kvsplit { _p: [u8; 0] }
+pub const BML_KVSPLIT_HANDLE_BYTES: usize = 64;
 #[repr(C)] pub struct bml_gguf_header {
     pub magic: u32, pub version: u32, pub tensor_count: u64, pub metadata_kv_count: u64,
     pub data_offset: u64, pub file_size: u64,
@@ -88,6 +90,14 @@ extern "C" {
                            stream: *mut c_void) -> bml_status;
     pub fn bml_attn_workspace_check(ws: *mut c_void, bytes: usize, stream: *mut c_void) -> bml_status;
     pub fn bml_attn_noalloc_check(stream: *mut c_void) -> bml_status;
+    pub fn bml_kvsplit_create(device: i32, rank: u32, world: u32, n_heads: u32, head_dim: u32,
+                              out: *mut *mut bml_kvsplit) -> bml_status;
+    pub fn bml_kvsplit_handle(h: *const bml_kvsplit, handle: *mut c_void, bytes: usize) -> bml_status;
+    pub fn bml_kvsplit_open(h: *mut bml_kvsplit, handles: *const c_void, bytes: usize) -> bml_status;
+    pub fn bml_attn_decode_kvsplit(h: *mut bml_kvsplit, slice: *const bml_seq_desc, n_heads: u32, n_kv: u32,
+                                   head_dim: u32, kv: bml_dtype, scale: f32, q: *const f32, out: *mut f32,
+                                   ws: *mut c_void, ws_bytes: usize, stream: *mut c_void) -> bml_status;
+    pub fn bml_kvsplit_destroy(h: *mut bml_kvsplit) -> bml_status;
 
     // include/bml_weights.h -- read_tensor_f32 / matmul_f64 on the device
     pub fn bml_read_tensor_f32(data: *const c_void, data_len: u64, gguf_type: i32, n_elems: u64,

@@ -344,6 +344,45 @@ bml_status bml_softmax_f32(const float *x_dev, uint32_t n_rows, uint32_t n,
                            float *out_dev, void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* KV split of one sequence over GPUs                                       */
+/* ------------------------------------------------------------------------ */
+
+/* One long sequence whose KV cache is cut into contiguous slices, one per
+ * GPU (one process per GPU).  No reference counterpart: the reference runs
+ * the whole loop of gguf_compiler.rs:1026-1049 in one thread.  Every rank
+ * decodes its slice and, inside the same kernel, exchanges per-(q head, 32
+ * dims) partials (max, sum, normalised output) with every other rank over
+ * peer memory (CUDA IPC mappings, plain loads and stores) and merges them
+ * in rank order with the log-sum-exp rule; every rank ends with the same
+ * output.  Set-up: bml_kvsplit_create on each rank, bml_kvsplit_handle ->
+ * BML_KVSPLIT_HANDLE_BYTES bytes, gathered from all ranks in rank order
+ * (any host channel), bml_kvsplit_open.  All ranks must then call
+ * bml_attn_decode_kvsplit the same number of times with the same shape;
+ * a rank whose peers do not arrive within 2 s stops waiting and records
+ * BML_E_TIMEOUT in the workspace's error word (bml_attn_workspace_check). */
+typedef struct bml_kvsplit bml_kvsplit;
+#define BML_KVSPLIT_HANDLE_BYTES 64
+
+bml_status bml_kvsplit_create(int32_t device, uint32_t rank, uint32_t world,
+                              uint32_t n_heads, uint32_t head_dim,
+                              bml_kvsplit **out);
+bml_status bml_kvsplit_handle(const bml_kvsplit *h, void *handle_out,
+                              size_t bytes);
+bml_status bml_kvsplit_open(bml_kvsplit *h, const void *handles,
+                            size_t bytes);
+/* slice_host: this rank's slice of the cache (one descriptor, its own
+ * positions only); q_dev [n_heads][head_dim] f32, the same on every rank;
+ * out_dev [n_heads][head_dim] f32.  16-bit caches with the decode kernel's
+ * shapes.  Asynchronous. */
+bml_status bml_attn_decode_kvsplit(bml_kvsplit *h, const bml_seq_desc *slice_host,
+                                   uint32_t n_heads, uint32_t n_kv_heads,
+                                   uint32_t head_dim, bml_dtype kv_dtype,
+                                   float scale, const float *q_dev,
+                                   float *out_dev, void *workspace,
+                                   size_t workspace_bytes, void *stream);
+bml_status bml_kvsplit_destroy(bml_kvsplit *h);
+
+/* ------------------------------------------------------------------------ */
 /* Device-side error word                                                   */
 /* ------------------------------------------------------------------------ */
 
