@@ -450,34 +450,23 @@ struct BulkPlan {
 BulkPlan bulk_plan(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, uint32_t nph, uint32_t parts_per_seq,
                    int grid) {
     BulkPlan b;
+    const uint32_t nw = bml::decode_bulk_warps(head_dim);  // consumer warps
     const uint32_t per_row = std::min<uint32_t>(parts_per_seq, (uint32_t)grid / n_seqs + 2u) * nph;
     uint32_t wpr = 1;
-    while (wpr < 8 && per_row > 16u * wpr) wpr *= 2;
-    uint32_t rows = 8u / wpr;
-    if (wpr == 1 && n_heads % 16u == 0 && (uint64_t)n_seqs * n_heads / 8u > (uint64_t)grid) rows = 16;
+    while (wpr < nw && per_row > 16u * wpr) wpr *= 2;
+    uint32_t rows = nw / wpr;
+    if (wpr == 1 && n_heads % (2u * nw) == 0 && (uint64_t)n_seqs * n_heads / nw > (uint64_t)grid) rows = 2u * nw;
     while (rows > 1 && n_heads % rows) rows /= 2;  // small head counts
-    if (rows * wpr < 8u) wpr = 8u / rows;
+    if (rows * wpr < nw) wpr = nw / rows;
     b.merge_rows = rows;
     b.merge_wpr = wpr;
     // few rows with many slots each (a long sequence): split the head dims
     // too, so that more CTAs share the merge and each lane keeps all its
     // slots in flight at once
-    while (b.merge_dsplit < 4 && wpr == 8 && 32u * b.merge_dsplit * 2u <= head_dim &&
+    while (b.merge_dsplit < 4 && wpr == nw && 32u * b.merge_dsplit * 2u <= head_dim &&
            (uint64_t)n_seqs * (n_heads / rows) * b.merge_dsplit * 2u <= (uint64_t)grid)
         b.merge_dsplit *= 2;
     return b;
-}
-
-// Home CTAs of the busiest sequence of a claimed-schedule launch (each takes
-// one part of it statically).
-uint32_t max_homes(const bml::DecodeParams &p, uint32_t total, uint32_t grid) {
-    uint32_t m = 0;
-    for (uint32_t s = 0; s < p.n_seqs; ++s) {
-        const uint32_t lo = bml::decode_home_lo(p.seqs[s].tile_begin, total, grid);
-        const uint32_t hi = s + 1 < p.n_seqs ? bml::decode_home_lo(p.seqs[s + 1].tile_begin, total, grid) : grid;
-        m = std::max(m, hi - lo);
-    }
-    return m;
 }
 
 // A KV split over GPUs: this rank, the call's epoch and every rank's
@@ -531,6 +520,7 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
         memset(&p, 0, offsetof(bml::DecodeParams, seqs));
         p.n_seqs = ns;
         p.n_kv = n_kv;
+        p.rows_per_tile = T;  // the schedule below counts tiles with it
         uint64_t total = 0;
         uint32_t slot = 0, max_slots_seq = 0;
         for (uint32_t s = 0; s < ns; ++s) {
@@ -551,11 +541,11 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
             // at least the busiest sequence's home CTAs (fewer CTAs if the
             // slots are short).
             grid = (int)std::min<uint64_t>((uint64_t)sms, total);
-            const uint32_t nph = bml::decode_bulk_phases(n_kv);
+            const uint32_t nph = bml::decode_bulk_phases(n_kv, head_dim);
             size_t pps = 0;
             while (true) {
                 pps = std::min<size_t>({(size_t)grid, ws.max_slots / ((size_t)ns * nph), bml::kMaxPartTiles / ns});
-                if (pps >= std::max<uint32_t>(1u, max_homes(p, (uint32_t)total, (uint32_t)grid)) || grid == 1) break;
+                if (pps >= std::max<uint32_t>(1u, bml::decode_assign_homes(p, (uint32_t)grid)) || grid == 1) break;
                 grid = std::max(1, grid * 3 / 4);
             }
             if (pps == 0) return fail(BML_E_INVALID, "%s: internal part overflow", fn);
@@ -568,7 +558,7 @@ bml_status decode_impl(const bml_seq_desc *seqs, uint32_t n_seqs, uint32_t n_hea
             p.merge_dsplit = plan.merge_dsplit;
             if (split) {  // one merge item per exchange unit: a row x 32 dims
                 p.merge_rows = 1;
-                p.merge_wpr = 8;
+                p.merge_wpr = bml::decode_bulk_warps(head_dim);
                 p.merge_dsplit = head_dim / 32;
                 p.x_world = xa->world;
                 p.x_rank = xa->rank;

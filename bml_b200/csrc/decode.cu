@@ -748,8 +748,8 @@ size_t decode_workspace_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t head_d
 size_t decode_workspace_min_bytes(uint32_t n_seqs, uint32_t n_heads, uint32_t n_kv, uint32_t head_dim,
                                   int num_sms) {
     // the static schedule's split points, and one part of every sequence of
-    // a claimed-schedule launch (8 / n_kv slots a part)
-    const size_t nph = n_kv && n_kv <= 8 ? 8 / n_kv : 8;
+    // a claimed-schedule launch (one slot per consumer warp of a kv head)
+    const size_t nph = n_kv && n_kv <= 8 ? decode_bulk_warps(head_dim) / n_kv : 16;
     return workspace_bytes_for(std::max<size_t>(2 * launch_seqs(n_seqs) + (size_t)num_sms,
                                                 nph * launch_seqs(n_seqs)),
                                n_heads, head_dim);

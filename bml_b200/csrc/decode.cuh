@@ -10,15 +10,16 @@ namespace bml {
 // [b*tiles_per_cta, (b+1)*tiles_per_cta); tile_begin is the sequence's first
 // global tile and its n_slots partial slots are one per CTA touching it.
 // Claimed schedule (decode_bulk_kernel): tile_begin is the sequence's first
-// global tile (prefix of the tile counts); CTAs claim the sequence's tiles
-// at run time and leave at most parts_per_seq parts of it.
+// global tile (prefix of the tile counts); slot_base / n_slots are the first
+// of its home CTAs and their number (decode_assign_homes); CTAs claim the
+// sequence's tiles at run time and leave at most parts_per_seq parts of it.
 struct DecodeSeq {
     const void *k;        // [len][n_kv][D]
     const void *v;
     uint32_t len;         // positions attended
     uint32_t tile_begin;  // first global tile of this sequence
-    uint32_t slot_base;   // static schedule: first partial slot of this sequence
-    uint32_t n_slots;     // static schedule: CTAs touching this sequence
+    uint32_t slot_base;   // static: first partial slot; claimed: first home CTA
+    uint32_t n_slots;     // static: CTAs touching it; claimed: home CTAs
 };
 
 constexpr int kMaxSeqsPerLaunch = 256;
@@ -125,25 +126,32 @@ cudaError_t launch_decode(const DecodeParams &p, bml_dtype dt, uint32_t head_dim
 bool decode_bulk_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group);
 cudaError_t launch_decode_bulk(const DecodeParams &p, bml_dtype dt, uint32_t head_dim, uint32_t group,
                                int grid, cudaStream_t stream);
-// Claimed schedule: CTA b's home sequence holds tile ((2b + 1) * total) /
-// (2 * grid); this is the first CTA whose home is a sequence starting at
-// global tile `tile_begin` (the home CTAs of a sequence are a contiguous
-// range).  Home CTAs of a sequence take its first tiles and parts statically,
-// one each, so a launch issues its first copies without waiting on an atomic.
-__host__ __device__ inline uint32_t decode_home_lo(uint32_t tile_begin, uint32_t total, uint32_t grid) {
-    const uint64_t need = 2ull * grid * tile_begin;
-    if (need <= total) return 0;
-    const uint64_t num = need - total, den = 2ull * total;
-    const uint64_t b = (num + den - 1) / den;
-    return b < grid ? (uint32_t)b : grid;
-}
+// Claimed schedule: deals the grid's CTAs to the sequences of p as home
+// CTAs (contiguous ranges in sequence order, seqs[].slot_base / n_slots) so
+// that the largest home load, tiles per home CTA, is as small as it can be:
+// one home for each sequence (longest first, while CTAs last), then each
+// further CTA to the sequence with the most tiles per home; never more homes
+// than tiles.  Home CTAs take a sequence's first tiles and parts statically,
+// one each, so a launch issues its first copies without waiting on an
+// atomic.  Returns the most homes any sequence got.  Measured on B200: the
+// even spacing it replaces (CTA b's home held tile (b + 1/2) * total / grid)
+// gave a 27-tile sequence of the ragged TinyLlama-shaped batch one home CTA
+// against an average of 15.3 tiles, and that CTA set the batch's time.
+uint32_t decode_assign_homes(DecodeParams &p, uint32_t grid);
 
 // Parts of a claimed-schedule launch (n_seqs * parts_per_seq) are limited
 // by the fixed part-tile area of a workspace.
 constexpr size_t kMaxPartTiles = 16384;
+// Consumer warps of decode_bulk_kernel: 16 for head_dim 64 (tiles of 64
+// positions carry twice the MMA work per byte of head_dim 128, and a warp's
+// dependent chain per tile is what limits them: measured on B200, 8 warps
+// streamed the ragged TinyLlama-shaped batch at ~4.6 TB/s against 7.3 for
+// head_dim 128), 8 otherwise (the register budget of 17 warps, 96 a
+// thread, does not hold the head_dim-128 state).
+__host__ __device__ constexpr uint32_t decode_bulk_warps(uint32_t head_dim) { return head_dim == 64 ? 16u : 8u; }
 // Partial slots a q head row of a sequence leaves per part: the consumer
-// warps serving one kv head (8 / n_kv).
-inline uint32_t decode_bulk_phases(uint32_t n_kv) { return 8u / n_kv; }
+// warps serving one kv head.
+inline uint32_t decode_bulk_phases(uint32_t n_kv, uint32_t head_dim) { return decode_bulk_warps(head_dim) / n_kv; }
 
 // Merge of split-K slots for sequences spread over more CTAs than the
 // in-kernel merge handles well; one CTA per (sequence, head) row.

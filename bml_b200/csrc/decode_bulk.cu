@@ -26,9 +26,10 @@
 // the tiles leaves the last CTA finishing ~40% after the median one, and a
 // partial per fixed-size chunk costs either balance (large chunks) or
 // partial traffic and a separate merge launch (small ones).  Here:
-//  * CTA b's home sequence holds tile (b + 1/2) * total / grid; the home CTAs
-//    of a sequence take its first tiles and its first parts statically, one
-//    each, so every CTA issues its first copy without waiting on an atomic;
+//  * the host deals the CTAs to the sequences as home CTAs (fewest tiles per
+//    home CTA at worst, decode_assign_homes); the home CTAs of a sequence
+//    take its first tiles and its first parts statically, one each, so every
+//    CTA issues its first copy without waiting on an atomic;
 //    further tiles are claimed claim_tiles at a time from a per-sequence
 //    counter (the producer claims one claim ahead, hiding the atomic);
 //  * a CTA carries its running (m, l, o) over every tile it takes of a
@@ -52,15 +53,17 @@
 // with the reference to the decode tolerance but may differ between runs in
 // the last bits.
 //
-// Roles (warp specialisation): warp 8 is the producer -- lane 0 claims tiles
-// and reserves parts, the warp picks the next sequence (one counter per
-// lane), lanes 0-15 issue the group copies -- over a 3-stage ring whose
+// Roles (warp specialisation): warp NW is the producer -- lane 0 claims
+// tiles and reserves parts, the warp picks the next sequence (one counter
+// per lane), lanes 0-15 issue the group copies -- over a 3-stage ring whose
 // stages are tiles or control records (visit start, flush, end), released
-// through `empty` barriers; warps 0-7 consume: warp w serves kv head w %
-// n_kv and the m-tiles w / n_kv (mod 8 / n_kv) of every tile, and at a flush
-// writes its own partial for its heads (8 / n_kv partial slots a part) with
-// no CTA-wide barrier.
+// through `empty` barriers; warps 0..NW-1 consume (NW = 8 for head_dim 128,
+// 16 for 64): warp w serves kv head w % n_kv and the m-tiles w / n_kv (mod
+// NW / n_kv) of every tile, and at a flush writes its own partial for its
+// heads (NW / n_kv partial slots a part) with no CTA-wide barrier.
 #include <math.h>
+
+#include <algorithm>
 
 #include "decode.cuh"
 #include "mma_frag.cuh"
@@ -70,21 +73,23 @@ namespace bml {
 namespace {
 
 constexpr int kSmemBudget = 227 * 1024;
-constexpr int kWarps = 8;                    // consumer warps
-constexpr int kThreads = (kWarps + 1) * 32;  // + the producer warp
 constexpr int kStageK = 32768;               // K bytes of a full tile (V the same)
 constexpr int kStages = 3;
 constexpr float kRescaleThreshold = 8.0f;
 constexpr unsigned kFull = 0xffffffffu;
 constexpr uint32_t kNone = 0xffffffffu;
 
-template <int D, int G>
+// NW consumer warps (decode_bulk_warps: 8 for head_dim 128, 16 for 64) + one
+// producer warp.
+template <int D, int G, int NW>
 struct BCfg {
+    static constexpr int THREADS = (NW + 1) * 32;
     static constexpr int NT = (2 * G + 7) / 8;  // n8 column tiles of S (4 heads each)
     static constexpr int KS = D / 16;           // k-steps of S, d-blocks of O^T
-    static constexpr int MTW = 128 / D;         // m-tiles per warp per tile
+    static constexpr int MTW = 1024 / (D * NW);  // m-tiles per warp per tile
     static constexpr int SCR = 256;             // barriers, flags, stage records
-    static constexpr int MERGE = kWarps * (D + 4) * 4;  // merge scratch: per warp (M, L, -, -, O[D])
+    static constexpr int MERGE = NW * (D + 4) * 4;  // merge scratch: per warp (M, L, -, -, O[D])
+    static_assert(MTW >= 1, "at most one warp per m-tile");
 };
 
 // Bytes of one K (or V) tile of T rows: eight groups at pitch
@@ -93,35 +98,30 @@ __host__ __device__ __forceinline__ uint32_t ktile_bytes_of(uint32_t T, uint32_t
     return T * row_bytes + 128u;
 }
 
-template <int D, int G>
+template <int D, int G, int NW>
 uint32_t smem_bytes(uint32_t T, uint32_t row_bytes) {
-    // the merge stages its slots in the ring: 8 warps' batches fit in it
-    static_assert(kWarps * 32u * (D + 3u) * 4u <= kStages * 2u * 32768u, "merge staging exceeds the ring");
-    return kStages * 2u * ktile_bytes_of(T, row_bytes) + BCfg<D, G>::SCR + BCfg<D, G>::MERGE + 128u;
-}
-
-// Sequence holding global tile t (binary search over the tile prefix).
-__device__ __forceinline__ uint32_t seq_of_tile(const DecodeParams &p, uint32_t t) {
-    uint32_t lo = 0, hi = p.n_seqs - 1;
-    while (lo < hi) {
-        const uint32_t mid = (lo + hi + 1) >> 1;
-        if (p.seqs[mid].tile_begin <= t) lo = mid; else hi = mid - 1;
-    }
-    return lo;
+    // the merge stages its slots in the ring: every warp's batch fits in it
+    static_assert(NW * 32u * (D + 3u) * 4u <= kStages * 2u * 32768u, "merge staging exceeds the ring");
+    return kStages * 2u * ktile_bytes_of(T, row_bytes) + BCfg<D, G, NW>::SCR + BCfg<D, G, NW>::MERGE + 128u;
 }
 
 __device__ __forceinline__ uint32_t tiles_of(const DecodeParams &p, uint32_t s) {
     return (p.seqs[s].len + p.rows_per_tile - 1) / p.rows_per_tile;
 }
 
-// First CTA whose home is sequence s (gridDim.x past the last sequence).
-__device__ __forceinline__ uint32_t home_lo(const DecodeParams &p, uint32_t s) {
-    return s < p.n_seqs ? decode_home_lo(p.seqs[s].tile_begin, p.total_tiles, gridDim.x) : gridDim.x;
-}
+// Home CTAs of sequence s (decode_assign_homes): they hold its first tiles
+// and parts.
+__device__ __forceinline__ uint32_t homes_of(const DecodeParams &p, uint32_t s) { return p.seqs[s].n_slots; }
 
-// Home CTAs of sequence s: they hold its first tiles and parts.
-__device__ __forceinline__ uint32_t homes_of(const DecodeParams &p, uint32_t s) {
-    return home_lo(p, s + 1) - home_lo(p, s);
+// The home sequence of CTA b: the last sequence whose first home CTA is at
+// or before b (sequences without homes share the next one's first CTA).
+__device__ __forceinline__ uint32_t home_of_cta(const DecodeParams &p, uint32_t b) {
+    uint32_t lo = 0, hi = p.n_seqs - 1;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi + 1) >> 1;
+        if (p.seqs[mid].slot_base <= b) lo = mid; else hi = mid - 1;
+    }
+    return lo;
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long *p) {
@@ -350,7 +350,7 @@ __device__ __noinline__ void exchange_store(const DecodeParams &p, uint32_t unit
 // combine has a named barrier).  `stage` is the ring's shared memory, idle
 // once the stream has ended.  Not inlined, so that it takes no registers
 // from the streaming loop.
-template <int D, int VS, int RW>
+template <int D, int VS, int RW, int NW>
 __device__ __noinline__ void merge_item(const DecodeParams &p, uint32_t sq, uint32_t row0, uint32_t dim0,
                                            uint32_t nsub, uint32_t nph, uint32_t wpr, int warp, int lane,
                                            float *mscr, uint8_t *stage) {
@@ -370,7 +370,7 @@ __device__ __noinline__ void merge_item(const DecodeParams &p, uint32_t sq, uint
         }
 #pragma unroll
         for (int e = 0; e < VS; ++e) mine[4 + lane * VS + e] = O[0][e];
-        named_bar_sync(1, kWarps * 32);
+        named_bar_sync(1, NW * 32);
         if (sub == 0) {
             float Mt = NEG_INF;
             for (uint32_t i = 0; i < wpr; ++i) Mt = fmaxf(Mt, mscr[(warp + i) * (D + 4)]);
@@ -404,9 +404,10 @@ struct StageInfo {
 constexpr uint32_t kTile = 0u, kVisit = 1u, kFlush = 2u, kEnd = 3u;
 
 // ----------------------------------------------------------------- kernel
-template <int D, int G, bool F16>
-__global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_constant__ DecodeParams p) {
-    using C = BCfg<D, G>;
+template <int D, int G, bool F16, int NW>
+__global__ void __launch_bounds__(BCfg<D, G, NW>::THREADS, 1)
+    decode_bulk_kernel(const __grid_constant__ DecodeParams p) {
+    using C = BCfg<D, G, NW>;
     constexpr int NT = C::NT, KS = C::KS, MTW = C::MTW;
     constexpr float NEG_INF = -INFINITY;
 
@@ -426,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
     // [0] abort, [1] merge item, [2] merge parts, [3] last CTA to leave
     volatile uint32_t *flags = reinterpret_cast<volatile uint32_t *>(full + 8);
     volatile StageInfo *info = reinterpret_cast<volatile StageInfo *>(full + 12);  // [kStages]
-    float *mscr = reinterpret_cast<float *>(scr + C::SCR);    // [kWarps][D + 4]
+    float *mscr = reinterpret_cast<float *>(scr + C::SCR);    // [NW][D + 4]
 
     // per sequence: tiles claimed past the home tiles, and a state word whose
     // high half counts joining visits' part reservations and low half the
@@ -437,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
     uint32_t *const left_c = p.counters + 4 * kMaxSeqsPerLaunch;  // visits that ended
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t nph = kWarps / p.n_kv;  // warps per kv head = partial slots per part
+    const uint32_t nph = NW / p.n_kv;  // warps per kv head = partial slots per part
     const uint32_t U = p.claim_tiles;
     const uint32_t R = p.merge_rows, wpr = p.merge_wpr, DS = p.merge_dsplit;
     const uint32_t ips = p.n_heads / R * DS;  // merge items per sequence
@@ -446,14 +447,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kWarps);
+            mbar_init(&empty[i], NW);
         }
         flags[0] = 0u;
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == kWarps) {
+    if (warp == NW) {
         // ------------------------------------------------------- producer
         const uint64_t pol = l2_policy_evict_first();
         uint32_t it = 0;  // stages posted
@@ -576,9 +577,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
         bool run = (p.diag & kDiagStall) == 0u;
         if (run) {
             // the home visit: first tile and part by rank among the home CTAs
-            const uint32_t home = seq_of_tile(
-                p, (uint32_t)(((2ull * blockIdx.x + 1ull) * p.total_tiles) / (2ull * gridDim.x)));
-            const uint32_t r = blockIdx.x - home_lo(p, home);
+            const uint32_t home = home_of_cta(p, blockIdx.x);
+            const uint32_t r = blockIdx.x - p.seqs[home].slot_base;
             s = home;
             part = home * p.parts_per_seq + r;
             c = r;
@@ -727,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
                 // the warp whose count completes the sequence queues it for
                 // the merge
                 const unsigned long long old = atomicAdd(&state[seq], (unsigned long long)tiles);
-                if ((uint32_t)old + tiles == 8u * tiles_of(p, seq))
+                if ((uint32_t)old + tiles == (uint32_t)NW * tiles_of(p, seq))
                     st_release_gpu(&queue[atomicAdd(&p.sched[2], 1u)], seq + 1u);
             }
         };
@@ -886,28 +886,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
         // and passed with the end record, each further one by thread 0 after
         // the current one.  Item piece k = item % ips of a sequence is row
         // block k / DS (R rows) and head-dim slice k % DS (D / DS dims).
-        const uint32_t rw = R * wpr / kWarps;  // rows per warp: 1 or 2
+        const uint32_t rw = R * wpr / NW;  // rows per warp: 1 or 2
         if (threadIdx.x == 0) {
             flags[1] = flags[0] ? kNoItem : end_item;
             flags[2] = end_np;
             flags[4] = end_seq;
         }
-        named_bar_sync(1, kWarps * 32);
+        named_bar_sync(1, NW * 32);
         while (true) {
             const uint32_t item = flags[1], np = flags[2], sq = flags[4];
-            named_bar_sync(1, kWarps * 32);  // read before thread 0 writes the next
+            named_bar_sync(1, NW * 32);  // read before thread 0 writes the next
             if (item >= items) break;
             const uint32_t k = item % ips;
             const uint32_t row0 = k / DS * R, dim0 = k % DS * (D / DS);
             const uint32_t nsub = np * nph;
             if (rw == 2)
-                merge_item<D, D / 32, 2>(p, sq, row0, 0u, nsub, nph, 1u, warp, lane, mscr, stages);
+                merge_item<D, D / 32, 2, NW>(p, sq, row0, 0u, nsub, nph, 1u, warp, lane, mscr, stages);
             else if (DS == 1)
-                merge_item<D, D / 32, 1>(p, sq, row0, 0u, nsub, nph, wpr, warp, lane, mscr, stages);
+                merge_item<D, D / 32, 1, NW>(p, sq, row0, 0u, nsub, nph, wpr, warp, lane, mscr, stages);
             else if (DS == 2)
-                merge_item<D, D / 64, 1>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr, stages);
+                merge_item<D, D / 64, 1, NW>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr, stages);
             else if constexpr (D >= 128)
-                merge_item<D, D / 128, 1>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr, stages);
+                merge_item<D, D / 128, 1, NW>(p, sq, row0, dim0, nsub, nph, wpr, warp, lane, mscr, stages);
             if (threadIdx.x == 0) {
                 uint32_t nxt = kNoItem, nseq = 0, nnp = 0;
                 if (!claim_item(p, state, queue, ips, items, flags, nxt, nseq, nnp)) nxt = kNoItem;
@@ -915,7 +915,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
                 flags[2] = nnp;
                 flags[4] = nseq;
             }
-            named_bar_sync(1, kWarps * 32);  // the next item is published; the merge scratch is free
+            named_bar_sync(1, NW * 32);  // the next item is published; the merge scratch is free
         }
     }
 
@@ -951,18 +951,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_bulk_kernel(const __grid_c
 // ----------------------------------------------------------------- host
 template <int D, int G, bool F16>
 cudaError_t launch_t(const DecodeParams &p, int grid, cudaStream_t stream) {
-    const uint32_t smem = smem_bytes<D, G>(p.rows_per_tile, p.row_bytes);
+    constexpr int NW = decode_bulk_warps(D);
+    const uint32_t smem = smem_bytes<D, G, NW>(p.rows_per_tile, p.row_bytes);
     if (smem > (uint32_t)kSmemBudget) return cudaErrorNotSupported;
     static bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(decode_bulk_kernel<D, G, F16>,
+        cudaError_t e = cudaFuncSetAttribute(decode_bulk_kernel<D, G, F16, NW>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    decode_bulk_kernel<D, G, F16><<<grid, kThreads, smem, stream>>>(p);
+    decode_bulk_kernel<D, G, F16, NW><<<grid, BCfg<D, G, NW>::THREADS, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -979,18 +980,53 @@ cudaError_t launch_g(const DecodeParams &p, uint32_t group, int grid, cudaStream
 
 }  // namespace
 
+uint32_t decode_assign_homes(DecodeParams &p, uint32_t grid) {
+    const uint32_t n = p.n_seqs;
+    uint32_t nt[kMaxSeqsPerLaunch], h[kMaxSeqsPerLaunch], order[kMaxSeqsPerLaunch];
+    for (uint32_t s = 0; s < n; ++s) {
+        nt[s] = (p.seqs[s].len + p.rows_per_tile - 1) / p.rows_per_tile;
+        h[s] = 0;
+        order[s] = s;
+    }
+    std::sort(order, order + n, [&](uint32_t a, uint32_t b) { return nt[a] != nt[b] ? nt[a] > nt[b] : a < b; });
+    uint32_t left = grid;
+    for (uint32_t i = 0; i < n && left; ++i, --left) h[order[i]] = 1;
+    // further CTAs, one at a time, to the most tiles per home (nt / h,
+    // compared as nt_a * h_b > nt_b * h_a; lowest index on ties)
+    while (left) {
+        uint32_t best = n;
+        for (uint32_t s = 0; s < n; ++s) {
+            if (h[s] == 0 || h[s] >= nt[s]) continue;
+            if (best == n || (uint64_t)nt[s] * h[best] > (uint64_t)nt[best] * h[s]) best = s;
+        }
+        if (best == n) break;  // every sequence has a home per tile
+        ++h[best];
+        --left;
+    }
+    uint32_t lo = 0, most = 0;
+    for (uint32_t s = 0; s < n; ++s) {
+        p.seqs[s].slot_base = lo;
+        p.seqs[s].n_slots = h[s];
+        lo += h[s];
+        most = std::max(most, h[s]);
+    }
+    return most;
+}
+
 bool decode_bulk_supported(bml_dtype dt, uint32_t head_dim, uint32_t n_kv, uint32_t group) {
     if (dt != BML_BF16 && dt != BML_F16) return false;
     if (head_dim != 64 && head_dim != 128) return false;
     if (group != 1 && group != 2 && group != 4 && group != 8) return false;
     if (n_kv != 1 && n_kv != 2 && n_kv != 4 && n_kv != 8) return false;
     // whole m-tiles: T = 32 KiB / row_bytes must be a multiple of 16 and
-    // split evenly over the 8 / n_kv warps of a kv head
+    // split evenly over the warps of a kv head
     const uint32_t row_bytes = n_kv * head_dim * 2;
     if (row_bytes < 512 || row_bytes > 2048) return false;
     const uint32_t T = kStageK / row_bytes;
-    if (T % 16 != 0 || (T / 16) % (kWarps / n_kv) != 0) return false;
-    const uint32_t smem = head_dim == 128 ? smem_bytes<128, 8>(T, row_bytes) : smem_bytes<64, 8>(T, row_bytes);
+    const uint32_t nw = decode_bulk_warps(head_dim);
+    if (T % 16 != 0 || nw % n_kv != 0 || (T / 16) % (nw / n_kv) != 0) return false;
+    const uint32_t smem = head_dim == 128 ? smem_bytes<128, 8, decode_bulk_warps(128)>(T, row_bytes)
+                                          : smem_bytes<64, 8, decode_bulk_warps(64)>(T, row_bytes);
     return smem <= (uint32_t)kSmemBudget;
 }
 
@@ -1008,23 +1044,27 @@ cudaError_t launch_decode_bulk(const DecodeParams &p, bml_dtype dt, uint32_t hea
     // one warp per row), whole items per sequence
     const uint32_t wpr = p.merge_wpr, R = p.merge_rows;
     const uint32_t DS = p.merge_dsplit;
-    if (!(wpr == 1 || wpr == 2 || wpr == 4 || wpr == 8) || !(R * wpr == (uint32_t)kWarps ||
-                                                            (wpr == 1 && R == 2u * kWarps)) ||
+    const uint32_t NW = decode_bulk_warps(head_dim);
+    if (!(wpr == 1 || wpr == 2 || wpr == 4 || wpr == 8 || wpr == 16) || wpr > NW ||
+        !(R * wpr == NW || (wpr == 1 && R == 2u * NW)) ||
         p.n_heads % R != 0 || !(DS == 1 || DS == 2 || DS == 4) || 32u * DS > head_dim ||
-        (DS > 1 && R * wpr != (uint32_t)kWarps))
+        (DS > 1 && R * wpr != NW))
         return cudaErrorInvalidValue;
     // a KV split over GPUs: one sequence, items of one row x 32 dims
     if (p.x_world > 1 && (p.x_world > (uint32_t)kMaxExchangeRanks || p.x_rank >= p.x_world || p.n_seqs != 1 ||
-                          p.mode != kModeFinal || DS * 32u != head_dim || wpr != (uint32_t)kWarps || R != 1 ||
+                          p.mode != kModeFinal || DS * 32u != head_dim || wpr != NW || R != 1 ||
                           p.x_units != p.n_heads * DS || p.x_epoch == 0))
         return cudaErrorInvalidValue;
-    // every home CTA's static part fits the parts of its sequence
+    // the home CTAs: contiguous ranges covering the grid, each home CTA's
+    // static tile and part inside its sequence
+    uint32_t lo = 0;
     for (uint32_t s = 0; s < p.n_seqs; ++s) {
-        const uint32_t lo = decode_home_lo(p.seqs[s].tile_begin, p.total_tiles, (uint32_t)grid);
-        const uint32_t hi = s + 1 < p.n_seqs ? decode_home_lo(p.seqs[s + 1].tile_begin, p.total_tiles, (uint32_t)grid)
-                                             : (uint32_t)grid;
-        if (hi - lo > p.parts_per_seq) return cudaErrorInvalidValue;
+        const DecodeSeq &q = p.seqs[s];
+        if (q.slot_base != lo || q.n_slots > p.parts_per_seq || q.n_slots > (q.len + p.rows_per_tile - 1) / p.rows_per_tile)
+            return cudaErrorInvalidValue;
+        lo += q.n_slots;
     }
+    if (lo != (uint32_t)grid) return cudaErrorInvalidValue;
     const bool f16 = dt == BML_F16;
     if (head_dim == 128) return f16 ? launch_g<128, true>(p, group, grid, stream) : launch_g<128, false>(p, group, grid, stream);
     return f16 ? launch_g<64, true>(p, group, grid, stream) : launch_g<64, false>(p, group, grid, stream);
