@@ -122,17 +122,53 @@ def host_threads() -> int:
 # clocks during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock, power and clock-event reasons of one GPU during the timed
+    region.  NVML is polled from a thread (about every millisecond), so even
+    a few-millisecond timed loop gets samples; without NVML, nvidia-smi's
+    200 ms sampling is the fallback.  Read-only: nothing is set."""
     FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
     def __init__(self, torch_index: int):
+        import threading
         self.proc = None
         self.t0 = self.t1 = None
+        self.samples = []  # (sm_mhz, max_mhz, power_w, reason bits)
+        self.stop_ev = threading.Event()
+        self.thread = None
         try:
             import torch
-            p = torch.cuda.get_device_properties(torch_index)
-            bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+            props = torch.cuda.get_device_properties(torch_index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        except Exception as e:
+            log("clock sampler unavailable:", e)
+            return
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self.stop_ev.is_set():
+                    if self.t0 is not None and self.t1 is None:
+                        try:
+                            self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)), smax,
+                                                 pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                                 int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))))
+                        except pynvml.NVMLError:
+                            pass
+                    time.sleep(0.0005)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception as e:  # no NVML: nvidia-smi
+            log("NVML unavailable, sampling with nvidia-smi:", e)
+        try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200", "-i", bus], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
@@ -147,6 +183,15 @@ class ClockSampler:
 
     def stop(self):
         import datetime
+        if self.thread is not None:
+            self.stop_ev.set()
+            self.thread.join(timeout=2)
+            sm = [x[0] for x in self.samples]
+            reasons = sorted({n for x in self.samples for bit, n in self.REASONS.items() if x[3] & bit})
+            return {"sm_mhz": statistics.median(sm) if sm else None,
+                    "sm_max_mhz": max(x[1] for x in self.samples) if sm else None,
+                    "power_w_max": round(max(x[2] for x in self.samples), 1) if sm else None,
+                    "reasons": reasons, "samples": len(sm), "source": "nvml"}
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         self.proc.terminate()
@@ -181,7 +226,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
                 "power_w_max": max(power) if power else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
