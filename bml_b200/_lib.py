@@ -104,6 +104,7 @@ SIGNATURES = {
     "bml_read_tensor_f32": (_st, [_vp, C.c_uint64, _i32, C.c_uint64, _vp, C.POINTER(C.c_uint64), _vp]),
     "bml_matmul_workspace_size": (_st, [C.c_uint64, C.POINTER(_sz)]),
     "bml_matmul_f64": (_st, [_vp, C.c_uint64, _i32, C.c_uint64, C.c_uint64, _vp, C.c_uint64, _vp, _vp, _sz, _vp]),
+    "bml_matmul_f64_static": (_st, [_vp, C.c_uint64, _i32, C.c_uint64, C.c_uint64, _vp, C.c_uint64, _vp, _vp, _sz, _vp]),
     # include/bml_gguf.h
     "bml_gguf_open": (_st, [C.c_char_p, C.POINTER(_vp)]),
     "bml_gguf_close": (_st, [_vp]),

@@ -1064,10 +1064,9 @@ BML_API bml_status bml_matmul_workspace_size(uint64_t n_out, size_t *bytes) {
     return ok();
 }
 
-BML_API bml_status bml_matmul_f64(const void *w_dev, uint64_t data_len, int32_t gguf_type, uint64_t n_in,
-                                  uint64_t n_out, const double *x_dev, uint64_t x_len, double *y_dev, void *workspace,
-                                  size_t ws_bytes, void *stream) {
-    const char *fn = "bml_matmul_f64";
+static bml_status matmul_impl(const char *fn, const void *w_dev, uint64_t data_len, int32_t gguf_type, uint64_t n_in,
+                              uint64_t n_out, const double *x_dev, uint64_t x_len, double *y_dev, void *workspace,
+                              size_t ws_bytes, bool static_weights, void *stream) {
     if (!gguf_type_read(gguf_type))
         return fail(BML_E_UNSUPPORTED, "%s: GGUF type %d (the reference reads F32, F16, Q4_0, Q8_0)", fn, gguf_type);
     if (n_out == 0) return ok();
@@ -1086,7 +1085,21 @@ BML_API bml_status bml_matmul_f64(const void *w_dev, uint64_t data_len, int32_t 
         return fail(BML_E_INVALID, "%s: workspace of %zu bytes, need %zu", fn, ws_bytes,
                     bml::gemv_workspace_bytes(n_out));
     CUDA_TRY(bml::gemv(w_dev, data_len, gguf_type, n_in, n_out, x_dev, x_len, y_dev, static_cast<double *>(workspace),
-                       sms, static_cast<cudaStream_t>(stream)),
+                       sms, static_weights, static_cast<cudaStream_t>(stream)),
              fn);
     return ok();
+}
+
+BML_API bml_status bml_matmul_f64(const void *w_dev, uint64_t data_len, int32_t gguf_type, uint64_t n_in,
+                                  uint64_t n_out, const double *x_dev, uint64_t x_len, double *y_dev, void *workspace,
+                                  size_t ws_bytes, void *stream) {
+    return matmul_impl("bml_matmul_f64", w_dev, data_len, gguf_type, n_in, n_out, x_dev, x_len, y_dev, workspace,
+                       ws_bytes, false, stream);
+}
+
+BML_API bml_status bml_matmul_f64_static(const void *w_dev, uint64_t data_len, int32_t gguf_type, uint64_t n_in,
+                                         uint64_t n_out, const double *x_dev, uint64_t x_len, double *y_dev,
+                                         void *workspace, size_t ws_bytes, void *stream) {
+    return matmul_impl("bml_matmul_f64_static", w_dev, data_len, gguf_type, n_in, n_out, x_dev, x_len, y_dev,
+                       workspace, ws_bytes, true, stream);
 }

@@ -229,7 +229,7 @@ struct StagedCfg {
     static constexpr uint32_t RS = RS_RAW < 8u ? 8u : (RS_RAW / 8u) * 8u;  // rows per stage
     static constexpr uint32_t XOFF = RS * SEG;        // the stage's RS values of x (f64) follow its rows
     static constexpr uint32_t STAGE = XOFF + RS * 8u;
-    static constexpr uint32_t SMEM = kRing * STAGE > 8u * 1024u * 4u ? kRing * STAGE : 8u * 1024u * 4u;
+    static constexpr uint32_t SMEM = kRing * STAGE > 8u * 1056u * 4u ? kRing * STAGE : 8u * 1056u * 4u;
 };
 
 __device__ __forceinline__ void cp8(uint32_t dst, const void *src) {
@@ -245,42 +245,27 @@ __device__ __forceinline__ void cp_wait() {
 }
 
 // acc[i] += x * (values 2i, 2i+1 of the one block at shared address blk),
-// in packed f32x2 arithmetic (each lane rounds as fmaf does).  A quantized
-// value becomes a float with one byte permute: its byte lane is moved into
-// the low mantissa byte of 2^23 (the float then reads 2^23 + q), and one
-// packed add removes the offset, exactly.
+// in packed f32x2 arithmetic (each lane rounds as fmaf does), for Q8_0, F16
+// and F32 (Q4_0 has its own kernel below).  A Q8_0 value becomes a float
+// with one byte permute: its byte lane is moved into the low mantissa byte
+// of 2^23 (the float then reads 2^23 + q), and one packed add removes the
+// offset, exactly.
 template <int QT>
 __device__ __forceinline__ void block_fma_smem(const uint8_t *blk, float x, float2 acc[16]) {
-    if constexpr (QT == kGgufQ4_0 || QT == kGgufQ8_0) {
+    if constexpr (QT == kGgufQ8_0) {
         const uint16_t *h = reinterpret_cast<const uint16_t *>(blk);
         const float xs = x * f16_bits_to_f32(h[0]);
         const float2 xs2 = make_float2(xs, xs);
-        if constexpr (QT == kGgufQ4_0) {
-            const float2 off = make_float2(-8388616.0f, -8388616.0f);  // 2^23 + 8
+        const float2 off = make_float2(-8388736.0f, -8388736.0f);  // 2^23 + 128
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {
-                // quant bytes 4m..4m+3; byte c holds values 2c (low nibble) and 2c+1
-                const uint32_t w = __byte_perm(h[1 + 2 * m], h[2 + 2 * m], 0x5410);
-                const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+        for (int m = 0; m < 8; ++m) {
+            // quant bytes 4m..4m+3 (values 4m..4m+3), int8 -> q + 128
+            const uint32_t w = __byte_perm(h[1 + 2 * m], h[2 + 2 * m], 0x5410) ^ 0x80808080u;
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const float2 q = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440 + b)),
-                                                 __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440 + b)));
-                    acc[4 * m + b] = __ffma2_rn(xs2, __fadd2_rn(q, off), acc[4 * m + b]);
-                }
-            }
-        } else {
-            const float2 off = make_float2(-8388736.0f, -8388736.0f);  // 2^23 + 128
-#pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                // quant bytes 4m..4m+3 (values 4m..4m+3), int8 -> q + 128
-                const uint32_t w = __byte_perm(h[1 + 2 * m], h[2 + 2 * m], 0x5410) ^ 0x80808080u;
-#pragma unroll
-                for (int b = 0; b < 4; b += 2) {
-                    const float2 q = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440 + b)),
-                                                 __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441 + b)));
-                    acc[2 * m + b / 2] = __ffma2_rn(xs2, __fadd2_rn(q, off), acc[2 * m + b / 2]);
-                }
+            for (int b = 0; b < 4; b += 2) {
+                const float2 q = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440 + b)),
+                                             __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441 + b)));
+                acc[2 * m + b / 2] = __ffma2_rn(xs2, __fadd2_rn(q, off), acc[2 * m + b / 2]);
             }
         }
     } else if constexpr (QT == kGgufF16) {
@@ -387,18 +372,212 @@ __global__ void __launch_bounds__(kGemvThreads, 4) gemv_staged_kernel(const uint
     }
     cp_wait<0>();
     __syncthreads();
-    // the 8 row phases of each column, summed in f64 in phase order
-    float *part = reinterpret_cast<float *>(sm);  // [8][1024]
+    // the 8 row phases of each column, summed in f64 in phase order; block
+    // cbl's 32 columns sit at word cbl * 33 of phase row rp, so the 32 lanes
+    // of a store (32 blocks) land in 32 banks
+    float *part = reinterpret_cast<float *>(sm);  // [8][32 * 33]
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-        part[rp * 1024 + cbl * 32 + 2 * i] = acc[i].x;
-        part[rp * 1024 + cbl * 32 + 2 * i + 1] = acc[i].y;
+        part[rp * 1056 + cbl * 33 + 2 * i] = acc[i].x;
+        part[rp * 1056 + cbl * 33 + 2 * i + 1] = acc[i].y;
     }
     __syncthreads();
     for (uint32_t c = tid; c < tile_blocks * 32u; c += kGemvThreads) {
         double sacc = 0.0;
 #pragma unroll
-        for (int k = 0; k < kGemvThreads / kTileBlocks; ++k) sacc += (double)part[k * 1024 + c];
+        for (int k = 0; k < kGemvThreads / kTileBlocks; ++k) sacc += (double)part[k * 1056 + (c >> 5) * 33 + (c & 31u)];
+        dst[(uint64_t)blockIdx.y * n_out + cb0 * 32 + c] = sacc;
+    }
+}
+
+// ---- staged GEMV for Q4_0: the same tiles, row ranges, row phases and
+// order of every sum as gemv_staged_kernel (so the same result bits as the
+// generic staged form), at a third of its device time on B200.
+//  * A thread owns a PAIR of adjacent blocks of the tile (36 bytes, 4-byte
+//    aligned at 36p) and one row phase: 16 pairs x 8 phases = 128 threads,
+//    64 f32 sums a thread; nine 4-byte shared loads bring a pair's two
+//    scales and 32 quant bytes.  Block 0's quant bytes 0, 1 and 14, 15
+//    share words with the scales and are gathered into one word by one byte
+//    permute; every other quant word is used as loaded, and which sum slot
+//    holds which column is fixed per thread and undone at the end.
+//  * A nibble at bits 4k..4k+3 of a word becomes a float with one LOP3
+//    (inline: the compiler splits the AND and the OR otherwise):
+//    OR-ing in the exponent of 2^(23-4k) makes the mantissa bit 4k weigh 1,
+//    so the float reads 2^(23-4k) + q exactly; one packed add of
+//    -(2^(23-4k) + 8) leaves q - 8, exactly, for each lane.  The two
+//    nibbles of a byte share one packed add and one packed FMA.
+//  * Stages of 32 rows, ONE stage ahead (a ring of two): every CTA of the
+//    one-wave grid keeps ~18 KB in flight, ~10 MB over the GPU, enough to
+//    stream HBM while the data arrive in about the order they are used.
+//    Measured on B200 (4096 x 14336): two or three stages ahead, or an L2
+//    prefetch of the whole range at the start, put all 33 MB in flight at
+//    once and made a CTA's first stage land after ~3.5-5.5 us instead of
+//    ~2-3 us (13.8 -> 14.6-16.3 us a launch pair); 16-row stages held too
+//    little in flight.  A row is copied by 4 threads, 9 16-byte chunks each
+//    at immediate offsets from one address (copy loops with a division per
+//    chunk cost ~1.8 us; one bulk copy per 576-byte row, or a 2-D tensor
+//    copy per stage, streamed no faster).
+//  * The weights of stage 0 are requested before griddepcontrol.wait, x and
+//    everything after it: launched as a programmatic dependent of the
+//    previous kernel (bml_matmul_f64_static), the first weight bytes stream
+//    while that kernel ends (~1.1 us of a launch pair measured); launched
+//    plainly the wait does nothing.
+//  * The phase sums go through shared memory with each pair's 64 columns
+//    at a 66-word stride: the 16 lanes of a half-warp's 64-bit store fill
+//    all 32 banks.  (An unpadded [8][1024] array made every store a 32-way
+//    conflict: 3.2 us of a 18 us launch.)
+constexpr int kQ4Threads = 128;
+constexpr int kQ4Pairs = kTileBlocks / 2;          // 16
+constexpr int kQ4Phases = kQ4Threads / kQ4Pairs;    // 8, as gemv_staged_kernel
+constexpr uint32_t kQ4Rows = 32;                    // rows a stage
+constexpr uint32_t kQ4Seg = kTileBlocks * 18u;      // 576 bytes of a row in a tile
+constexpr uint32_t kQ4XOff = kQ4Rows * kQ4Seg;      // the stage's x values (f64) follow its rows
+constexpr uint32_t kQ4Stage = kQ4XOff + kQ4Rows * 8u;
+constexpr uint32_t kQ4PartStride = 1056;            // words a phase row: 16 pairs x 66
+constexpr uint32_t kQ4Smem = 2 * kQ4Stage > 8 * kQ4PartStride * 4 ? 2 * kQ4Stage : 8 * kQ4PartStride * 4;
+
+// (a & M) | c in one LOP3.  Written as C, the AND and the OR compile to two
+// instructions (measured on B200 by instruction-class counters: 17 integer
+// instructions per quant word instead of 9), and the integer pipe is what
+// limits this kernel.
+template <uint32_t M>
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "n"(M), "r"(c));
+    return d;
+}
+
+// Exponent fields that make mantissa bit 4k weigh 1: 2^23, 2^19, 2^15, 2^11.
+struct Q4Magic {
+    uint32_t m0 = 0x4B000000u, m1 = 0x49000000u, m2 = 0x47000000u, m3 = 0x45000000u;
+};
+
+// acc[0..3] += xs * (q - 8) for the 8 nibbles of quant word w (byte c of w:
+// low nibble into acc[c].x, high nibble into acc[c].y).
+__device__ __forceinline__ void q4_word(uint32_t w, float2 xs2, float2 *acc, const Q4Magic &mg) {
+    const float2 off01 = make_float2(-8388616.0f, -524296.0f);  // -(2^23 + 8), -(2^19 + 8)
+    const float2 off23 = make_float2(-32776.0f, -2056.0f);      // -(2^15 + 8), -(2^11 + 8)
+    const uint32_t u = w >> 16;
+    float2 q;
+    q = make_float2(__uint_as_float(and_or<0x000Fu>(w, mg.m0)), __uint_as_float(and_or<0x00F0u>(w, mg.m1)));
+    acc[0] = __ffma2_rn(xs2, __fadd2_rn(q, off01), acc[0]);
+    q = make_float2(__uint_as_float(and_or<0x0F00u>(w, mg.m2)), __uint_as_float(and_or<0xF000u>(w, mg.m3)));
+    acc[1] = __ffma2_rn(xs2, __fadd2_rn(q, off23), acc[1]);
+    q = make_float2(__uint_as_float(and_or<0x000Fu>(u, mg.m0)), __uint_as_float(and_or<0x00F0u>(u, mg.m1)));
+    acc[2] = __ffma2_rn(xs2, __fadd2_rn(q, off01), acc[2]);
+    q = make_float2(__uint_as_float(and_or<0x0F00u>(u, mg.m2)), __uint_as_float(and_or<0xF000u>(u, mg.m3)));
+    acc[3] = __ffma2_rn(xs2, __fadd2_rn(q, off23), acc[3]);
+}
+
+// Quant byte held by sum slot s (0..15) of a pair's first block: slots 0-3
+// hold bytes 0, 1, 14, 15 (the gathered word), slots 4-15 bytes 2-13.  The
+// second block's slots 16-31 hold its bytes 0-15 in order.
+__device__ __forceinline__ uint32_t q4_slot_byte(uint32_t s) {
+    return s >= 16u ? s - 16u : s >= 4u ? s - 2u : (s < 2u ? s : s + 12u);
+}
+
+__global__ void __launch_bounds__(kQ4Threads, 4) gemv_q4_kernel(const uint8_t *__restrict__ w, uint64_t n_out,
+                                                               uint64_t rows, uint64_t rows_per_range,
+                                                               const double *__restrict__ x,
+                                                               double *__restrict__ dst) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int tid = threadIdx.x;
+    const uint32_t pr = (uint32_t)tid % kQ4Pairs, rp = (uint32_t)tid / kQ4Pairs;
+    const uint64_t n_cb = n_out / 32;
+    const uint64_t row_bytes = n_cb * 18u;
+    const uint64_t cb0 = (uint64_t)blockIdx.x * kTileBlocks;
+    const uint32_t tile_blocks = (uint32_t)(n_cb - cb0 < (uint64_t)kTileBlocks ? n_cb - cb0 : (uint64_t)kTileBlocks);
+    const uint32_t seg_chunks = tile_blocks * 18u / 16u;  // 36 for a whole tile
+    const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_range;
+    const uint64_t r1 = min(r0 + rows_per_range, rows);
+    const uint32_t n_stages = (uint32_t)((r1 - r0 + kQ4Rows - 1) / kQ4Rows);
+    const uint32_t smem0 = (uint32_t)__cvta_generic_to_shared(sm);
+    // this thread copies row cr of each stage, chunks cc, cc + 4, ...
+    const uint32_t cr = (uint32_t)tid / 4u, cc = (uint32_t)tid % 4u;
+    const uint8_t *src0 = w + cb0 * 18u + (uint64_t)cr * row_bytes + cc * 16u;
+
+    auto stage_rows = [&](uint32_t st) {
+        const uint64_t rb = r0 + (uint64_t)st * kQ4Rows;
+        return (uint32_t)(r1 - rb < (uint64_t)kQ4Rows ? r1 - rb : (uint64_t)kQ4Rows);
+    };
+    auto issue_w = [&](uint32_t st) {  // the stage's row segments
+        if (st >= n_stages) return;
+        const uint32_t nr = stage_rows(st);
+        if (cr >= nr) return;
+        const uint8_t *src = src0 + (r0 + (uint64_t)st * kQ4Rows) * row_bytes;
+        const uint32_t dst_s = smem0 + (st & 1u) * kQ4Stage + cr * kQ4Seg + cc * 16u;
+        if (seg_chunks == 36u) {
+#pragma unroll
+            for (uint32_t j = 0; j < 9; ++j) cp16(dst_s + 64u * j, src + 64u * j);
+        } else {
+            for (uint32_t c = cc; c < seg_chunks; c += 4u) cp16(dst_s + (c - cc) * 16u, src + (c - cc) * 16u);
+        }
+    };
+    auto issue_x = [&](uint32_t st) {  // the stage's x values, then the stage's copy group
+        if (st < n_stages && (uint32_t)tid < stage_rows(st))
+            cp8(smem0 + (st & 1u) * kQ4Stage + kQ4XOff + tid * 8u, x + r0 + (uint64_t)st * kQ4Rows + tid);
+        cp_commit();
+    };
+
+    float2 acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = make_float2(0.f, 0.f);
+    const Q4Magic mg;
+    auto pair_row = [&](const uint8_t *slot, uint32_t rr) {
+        const uint32_t *wd = reinterpret_cast<const uint32_t *>(slot + rr * kQ4Seg + pr * 36u);
+        uint32_t W[9];
+#pragma unroll
+        for (int i = 0; i < 9; ++i) W[i] = wd[i];
+        const float xf = (float)reinterpret_cast<const double *>(slot + kQ4XOff)[rr];
+        const float xs0 = xf * __low2float(*reinterpret_cast<const __half2 *>(&W[0]));
+        const float xs1 = xf * __high2float(*reinterpret_cast<const __half2 *>(&W[4]));
+        const float2 x0 = make_float2(xs0, xs0), x1 = make_float2(xs1, xs1);
+        q4_word(__byte_perm(W[0], W[4], 0x5432), x0, acc + 0, mg);
+        q4_word(W[1], x0, acc + 4, mg);
+        q4_word(W[2], x0, acc + 8, mg);
+        q4_word(W[3], x0, acc + 12, mg);
+        q4_word(W[5], x1, acc + 16, mg);
+        q4_word(W[6], x1, acc + 20, mg);
+        q4_word(W[7], x1, acc + 24, mg);
+        q4_word(W[8], x1, acc + 28, mg);
+    };
+
+    issue_w(0);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // x (and dst) belong to the previous kernel until here
+    issue_x(0);
+    for (uint32_t st = 0; st < n_stages; ++st) {
+        cp_wait<0>();     // stage st has landed (this thread's copies)
+        __syncthreads();  // ... and every thread's; the other slot was consumed at st - 1
+        issue_w(st + 1);
+        issue_x(st + 1);
+        const uint32_t nr = stage_rows(st);
+        if (pr * 2u < tile_blocks) {
+            const uint8_t *slot = sm + (st & 1u) * kQ4Stage;
+            if (nr == kQ4Rows) {
+#pragma unroll
+                for (uint32_t k = 0; k < kQ4Rows / kQ4Phases; ++k) pair_row(slot, rp + k * kQ4Phases);
+            } else {
+                for (uint32_t rr = rp; rr < nr; rr += kQ4Phases) pair_row(slot, rr);
+            }
+        }
+    }
+    cp_wait<0>();
+    __syncthreads();
+    // the 8 row phases of each column, summed in f64 in phase order; pair
+    // pr's 64 columns sit at word pr * 66 of phase row rp
+    float *part = reinterpret_cast<float *>(sm);
+#pragma unroll
+    for (uint32_t s = 0; s < 32; ++s) {
+        const uint32_t col = (s >= 16u ? 32u : 0u) + 2u * q4_slot_byte(s);
+        *reinterpret_cast<float2 *>(part + rp * kQ4PartStride + pr * 66u + col) = acc[s];
+    }
+    __syncthreads();
+    for (uint32_t c = tid; c < tile_blocks * 32u; c += kQ4Threads) {
+        const uint32_t o = (c >> 6) * 66u + (c & 63u);
+        double sacc = 0.0;
+#pragma unroll
+        for (int k = 0; k < kQ4Phases; ++k) sacc += (double)part[k * kQ4PartStride + o];
         dst[(uint64_t)blockIdx.y * n_out + cb0 * 32 + c] = sacc;
     }
 }
@@ -407,8 +586,12 @@ __global__ void __launch_bounds__(kGemvThreads, 4) gemv_staged_kernel(const uint
 // sums ranges g, g+8, g+16, ... of them in that order (8 loads in flight per
 // column instead of one), and the 8 group sums are added in group order: a
 // fixed association, so results do not vary between runs.
+// Launched as a programmatic dependent of the range kernel: its CTAs may
+// start while that kernel ends and wait here for its partials.
 __global__ void __launch_bounds__(256) gemv_reduce_kernel(const double *__restrict__ partial, uint32_t n_ranges,
                                                           uint64_t n_out, double *__restrict__ y) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     __shared__ double grp[8][33];
     const uint32_t c = threadIdx.x & 31, g = threadIdx.x >> 5;
     const uint64_t j = (uint64_t)blockIdx.x * 32 + c;
@@ -500,28 +683,65 @@ bool gemv_staged_ok(const void *w, uint64_t data_len, int gguf_type, uint64_t n_
 
 namespace {
 
-template <int QT>
-cudaError_t launch_staged(const uint8_t *w, uint64_t n_out, const GemvPlan &pl, const double *x, double *dst,
-                          cudaStream_t st) {
-    using Cf = StagedCfg<QT>;
-    static bool configured[64] = {false};
+// Sets the dynamic shared-memory limit of `kernel` once per device.
+template <typename K>
+cudaError_t configure_once(K kernel, uint32_t smem, bool *configured) {
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !configured[dev]) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(gemv_staged_kernel<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) configured[dev] = true;
-    }
+    if (dev >= 0 && dev < 64 && configured[dev]) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess && dev >= 0 && dev < 64) configured[dev] = true;
+    return e;
+}
+
+// Launch with the programmatic-stream-serialisation attribute when
+// `dependent`: the kernel may start before the previous kernel on the stream
+// has ended, and waits for it at its griddepcontrol.wait.
+template <typename... P, typename... A>
+cudaError_t launch_ex(void (*kernel)(P...), dim3 grid, dim3 block, uint32_t smem, cudaStream_t st, bool dependent,
+                      A... args) {
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = dependent ? 1 : 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <int QT>
+cudaError_t launch_staged(const uint8_t *w, uint64_t n_out, const GemvPlan &pl, const double *x, double *dst,
+                          bool early, cudaStream_t st) {
     const dim3 grid((unsigned)pl.col_tiles, pl.ranges);
-    gemv_staged_kernel<QT><<<grid, kGemvThreads, Cf::SMEM, st>>>(w, n_out, pl.rows, pl.rows_per_range, x, dst);
-    return cudaGetLastError();
+    if constexpr (QT == kGgufQ4_0) {
+        static bool configured[64] = {false};
+        const cudaError_t e = configure_once(gemv_q4_kernel, kQ4Smem, configured);
+        if (e != cudaSuccess) return e;
+        return launch_ex(gemv_q4_kernel, grid, dim3(kQ4Threads), kQ4Smem, st, early, w, n_out, pl.rows,
+                         pl.rows_per_range, x, dst);
+    } else {
+        using Cf = StagedCfg<QT>;
+        static bool configured[64] = {false};
+        const cudaError_t e = configure_once(gemv_staged_kernel<QT>, Cf::SMEM, configured);
+        if (e != cudaSuccess) return e;
+        gemv_staged_kernel<QT><<<grid, kGemvThreads, Cf::SMEM, st>>>(w, n_out, pl.rows, pl.rows_per_range, x, dst);
+        return cudaGetLastError();
+    }
+}
+
+cudaError_t launch_reduce(const double *partial, uint32_t ranges, uint64_t n_out, double *y, cudaStream_t st) {
+    return launch_ex(gemv_reduce_kernel, dim3((unsigned)((n_out + 31) / 32)), dim3(256), 0, st, true, partial, ranges,
+                     n_out, y);
 }
 
 }  // namespace
 
 cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in, uint64_t n_out, const double *x,
-                 uint64_t x_len, double *y, double *partial, int num_sms, cudaStream_t st) {
+                 uint64_t x_len, double *y, double *partial, int num_sms, bool static_weights, cudaStream_t st) {
     const bool staged = gemv_staged_ok(w, data_len, gguf_type, n_in, n_out);
     const GemvPlan pl = gemv_plan(n_in, n_out, x_len, num_sms, staged);
     if (pl.rows == 0) return cudaMemsetAsync(y, 0, n_out * sizeof(double), st);
@@ -538,15 +758,14 @@ cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in,
     if (staged) {
         cudaError_t se = cudaSuccess;
         switch (gguf_type) {
-            case kGgufF32: se = launch_staged<kGgufF32>(wb, n_out, pl, x, dst, st); break;
-            case kGgufF16: se = launch_staged<kGgufF16>(wb, n_out, pl, x, dst, st); break;
-            case kGgufQ4_0: se = launch_staged<kGgufQ4_0>(wb, n_out, pl, x, dst, st); break;
-            case kGgufQ8_0: se = launch_staged<kGgufQ8_0>(wb, n_out, pl, x, dst, st); break;
+            case kGgufF32: se = launch_staged<kGgufF32>(wb, n_out, pl, x, dst, static_weights, st); break;
+            case kGgufF16: se = launch_staged<kGgufF16>(wb, n_out, pl, x, dst, static_weights, st); break;
+            case kGgufQ4_0: se = launch_staged<kGgufQ4_0>(wb, n_out, pl, x, dst, static_weights, st); break;
+            case kGgufQ8_0: se = launch_staged<kGgufQ8_0>(wb, n_out, pl, x, dst, static_weights, st); break;
             default: return cudaErrorInvalidValue;
         }
         if (se != cudaSuccess || pl.ranges == 1) return se;
-        gemv_reduce_kernel<<<(unsigned)((n_out + 31) / 32), 256, 0, st>>>(partial, pl.ranges, n_out, y);
-        return cudaGetLastError();
+        return launch_reduce(partial, pl.ranges, n_out, y, st);
     }
     switch (gguf_type) {
         case kGgufF32: gemv_kernel<kGgufF32><<<grid, kGemvThreads, 0, st>>>(wb, n_ok, n_out, pl.rows, pl.rows_per_range, x, dst); break;
@@ -557,8 +776,7 @@ cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in,
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || pl.ranges == 1) return e;
-    gemv_reduce_kernel<<<(unsigned)((n_out + 31) / 32), 256, 0, st>>>(partial, pl.ranges, n_out, y);
-    return cudaGetLastError();
+    return launch_reduce(partial, pl.ranges, n_out, y, st);
 }
 
 }  // namespace bml

@@ -33,7 +33,10 @@ size_t gemv_workspace_bytes(uint64_t n_out);
 
 // y[j] = sum_i x[i] * W[i*n_out + j] over the tensor's values (see gemv.cu).
 // Quantized types need n_out % 32 == 0 (cudaErrorNotSupported otherwise).
+// static_weights: W is not written by the kernel launched just before on
+// the stream, so the Q4_0 kernel may be launched as its programmatic
+// dependent and start loading W while it ends (x and y wait for it).
 cudaError_t gemv(const void *w, uint64_t data_len, int gguf_type, uint64_t n_in, uint64_t n_out, const double *x,
-                 uint64_t x_len, double *y, double *partial, int num_sms, cudaStream_t st);
+                 uint64_t x_len, double *y, double *partial, int num_sms, bool static_weights, cudaStream_t st);
 
 }  // namespace bml

@@ -76,8 +76,15 @@ class WeightTensor:
     def to_f32(self, stream=None) -> torch.Tensor:
         return read_tensor_f32(self.data, self.gguf_type, self.n_elems, stream=stream)
 
-    def matmul_f64(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-        """y = x . W (gguf_compiler.rs:1239-1255); x, y f64 device vectors."""
+    def matmul_f64(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None,
+                   overlap: bool = True) -> torch.Tensor:
+        """y = x . W (gguf_compiler.rs:1239-1255); x, y f64 device vectors.
+
+        overlap: the tensor's bytes are not written by the kernel launched
+        just before (a WeightTensor's data is written once, by its upload),
+        so the call may start streaming them while that kernel ends
+        (bml_matmul_f64_static; same result bits).  False gives the plain
+        bml_matmul_f64."""
         if not isinstance(x, torch.Tensor) or not x.is_cuda or x.dtype != torch.float64 or not x.is_contiguous():
             raise ValueError("x must be a contiguous f64 CUDA vector")
         if out is None:
@@ -86,11 +93,13 @@ class WeightTensor:
             size = C.c_size_t()
             L.call("bml_matmul_workspace_size", self.n_out, C.byref(size))
             self._ws = torch.empty(size.value, dtype=torch.uint8, device=x.device)
-        L.call("bml_matmul_f64", C.c_void_p(self.data.data_ptr()), self.nbytes, self.gguf_type, self.n_in, self.n_out,
+        L.call("bml_matmul_f64_static" if overlap else "bml_matmul_f64", C.c_void_p(self.data.data_ptr()), self.nbytes,
+               self.gguf_type, self.n_in, self.n_out,
                C.c_void_p(x.data_ptr()), x.numel(), C.c_void_p(out.data_ptr()), C.c_void_p(self._ws.data_ptr()),
                self._ws.numel(), _stream(stream))
         return out
 
 
-def matmul_f64(w: WeightTensor, x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
-    return w.matmul_f64(x, out=out, stream=stream)
+def matmul_f64(w: WeightTensor, x: torch.Tensor, out: torch.Tensor | None = None, stream=None,
+               overlap: bool = True) -> torch.Tensor:
+    return w.matmul_f64(x, out=out, stream=stream, overlap=overlap)

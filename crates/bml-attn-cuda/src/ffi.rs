@@ -106,6 +106,9 @@ extern "C" {
     pub fn bml_matmul_f64(w: *const c_void, data_len: u64, gguf_type: i32, n_in: u64, n_out: u64,
                           x: *const f64, x_len: u64, y: *mut f64, ws: *mut c_void, ws_bytes: usize,
                           stream: *mut c_void) -> bml_status;
+    pub fn bml_matmul_f64_static(w: *const c_void, data_len: u64, gguf_type: i32, n_in: u64, n_out: u64,
+                                 x: *const f64, x_len: u64, y: *mut f64, ws: *mut c_void, ws_bytes: usize,
+                                 stream: *mut c_void) -> bml_status;
 
     // include/bml_gguf.h -- GgufParser + upload to the device
     pub fn bml_gguf_open(path: *const c_char, out: *mut *mut bml_gguf) -> bml_status;

@@ -64,6 +64,22 @@ bml_status bml_matmul_f64(const void *w_dev, uint64_t data_len,
                           const double *x_dev, uint64_t x_len, double *y_dev,
                           void *workspace, size_t ws_bytes, void *stream);
 
+/* bml_matmul_f64 with the same arguments and the same result bits, for a
+ * weight tensor that no kernel writes while calls are queued (weights
+ * uploaded once and read by many calls).  The call may start streaming W
+ * while the kernel launched just before it on `stream` is still running
+ * (CUDA programmatic dependent launch); x_dev is read and y_dev written
+ * only after that kernel has ended, so x may be that kernel's output.
+ * Back-to-back projections of a decode step overlap one's start with the
+ * previous one's end this way.  W must not be written by the kernel
+ * launched immediately before the call. */
+bml_status bml_matmul_f64_static(const void *w_dev, uint64_t data_len,
+                                 int32_t gguf_type, uint64_t n_in,
+                                 uint64_t n_out, const double *x_dev,
+                                 uint64_t x_len, double *y_dev,
+                                 void *workspace, size_t ws_bytes,
+                                 void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -108,6 +108,9 @@ def test_weight_path_rejects_on_host(L):
     assert lib.bml_matmul_f64(16, 18 * 8, L.GGUF_Q4_0, 16, 16, 16, 16, 16, None, 0, None) == L.BML_E_UNSUPPORTED
     # misaligned F32 weights
     assert lib.bml_matmul_f64(18, 64, L.GGUF_F32, 4, 4, 16, 4, 16, None, 0, None) == L.BML_E_INVALID
+    # the static-weights entry validates the same way
+    assert lib.bml_matmul_f64_static(16, 18 * 8, L.GGUF_Q4_0, 16, 16, 16, 16, 16, None, 0, None) == L.BML_E_UNSUPPORTED
+    assert lib.bml_matmul_f64_static(18, 64, L.GGUF_F32, 4, 4, 16, 4, 16, None, 0, None) == L.BML_E_INVALID
     size = C.c_size_t()
     assert lib.bml_matmul_workspace_size(4096, C.byref(size)) == L.BML_OK and size.value == 160 * 4096 * 8
 
