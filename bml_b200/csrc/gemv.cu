@@ -38,6 +38,7 @@ constexpr int kColBlocks = 8;                  // 32-column blocks per CTA
 constexpr int kCols = kColBlocks * 32;         // columns per CTA
 constexpr int kRowPhases = kGemvThreads / kColBlocks;  // 32
 constexpr uint64_t kMaxRanges = 160;                  // row ranges of one GEMV
+constexpr uint32_t kReduceLoads = (kMaxRanges + 7) / 8;  // ranges a reduce thread adds: 20
 
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
@@ -417,11 +418,11 @@ __global__ void __launch_bounds__(kGemvThreads, 4) gemv_staged_kernel(const uint
 //    at immediate offsets from one address (copy loops with a division per
 //    chunk cost ~1.8 us; one bulk copy per 576-byte row, or a 2-D tensor
 //    copy per stage, streamed no faster).
-//  * The weights of stage 0 are requested before griddepcontrol.wait, x and
-//    everything after it: launched as a programmatic dependent of the
-//    previous kernel (bml_matmul_f64_static), the first weight bytes stream
-//    while that kernel ends (~1.1 us of a launch pair measured); launched
-//    plainly the wait does nothing.
+//  * The weights of stage 0 may be requested before griddepcontrol.wait, x
+//    and everything else after it: launched as a programmatic dependent of
+//    the previous kernel (bml_matmul_f64_static), the first weight bytes
+//    stream while that kernel ends (~1.1 us of a 4096 x 14336 launch pair
+//    measured); launched plainly the wait does nothing.
 //  * The phase sums go through shared memory with each pair's 64 columns
 //    at a 66-word stride: the 16 lanes of a half-warp's 64-bit store fill
 //    all 32 banks.  (An unpadded [8][1024] array made every store a 32-way
@@ -542,9 +543,16 @@ __global__ void __launch_bounds__(kQ4Threads, 4) gemv_q4_kernel(const uint8_t *_
         q4_word(W[8], x1, acc + 28, mg);
     };
 
-    issue_w(0);
+    // Stage 0's weights go out before the wait only when the range has at
+    // least 3 stages: with one or two, stage 0 is most of the tensor, and
+    // loading it early only competes with the previous kernel's own stream
+    // (4096 x 4096, one stage a range: 6.7 us a launch pair without, 8.5
+    // with; 4096 x 14336, four stages: 14.0 without, 12.7 with).
+    const bool early = n_stages >= 3;
+    if (early) issue_w(0);
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // x (and dst) belong to the previous kernel until here
+    if (!early) issue_w(0);
     issue_x(0);
     for (uint32_t st = 0; st < n_stages; ++st) {
         cp_wait<0>();     // stage st has landed (this thread's copies)
@@ -583,11 +591,13 @@ __global__ void __launch_bounds__(kQ4Threads, 4) gemv_q4_kernel(const uint8_t *_
 }
 
 // y[j] = sum of the row ranges' partials.  A CTA takes 32 columns; warp g
-// sums ranges g, g+8, g+16, ... of them in that order (8 loads in flight per
-// column instead of one), and the 8 group sums are added in group order: a
-// fixed association, so results do not vary between runs.
-// Launched as a programmatic dependent of the range kernel: its CTAs may
-// start while that kernel ends and wait here for its partials.
+// sums ranges g, g+8, g+16, ... of them in that order, and the 8 group sums
+// are added in group order: a fixed association, so results do not vary
+// between runs.  A thread's (at most 20) loads are all issued before the
+// first add: with each add chained on its load the loop paid one L2 round
+// trip per range (the 148-range 14336 x 4096 projection: 17.2 -> 15.0 us a
+// launch pair).  Launched as a programmatic dependent of the range kernel:
+// its CTAs may start while that kernel ends and wait here for its partials.
 __global__ void __launch_bounds__(256) gemv_reduce_kernel(const double *__restrict__ partial, uint32_t n_ranges,
                                                           uint64_t n_out, double *__restrict__ y) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -595,9 +605,16 @@ __global__ void __launch_bounds__(256) gemv_reduce_kernel(const double *__restri
     __shared__ double grp[8][33];
     const uint32_t c = threadIdx.x & 31, g = threadIdx.x >> 5;
     const uint64_t j = (uint64_t)blockIdx.x * 32 + c;
+    double v[kReduceLoads];
+#pragma unroll
+    for (uint32_t k = 0; k < kReduceLoads; ++k) {
+        const uint32_t r = g + 8u * k;
+        v[k] = (j < n_out && r < n_ranges) ? partial[(uint64_t)r * n_out + j] : 0.0;
+    }
     double s = 0.0;
-    if (j < n_out)
-        for (uint32_t r = g; r < n_ranges; r += 8) s += partial[(uint64_t)r * n_out + j];
+#pragma unroll
+    for (uint32_t k = 0; k < kReduceLoads; ++k)
+        if (g + 8u * k < n_ranges) s += v[k];
     grp[g][c] = s;
     __syncthreads();
     if (g == 0 && j < n_out) {
