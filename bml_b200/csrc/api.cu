@@ -469,10 +469,11 @@ BulkPlan bulk_plan(uint32_t n_seqs, uint32_t n_heads, uint32_t head_dim, uint32_
     return b;
 }
 
-// A KV split over GPUs: this rank, the call's epoch and every rank's
-// exchange buffer (mapped into this process).
+// A KV split over GPUs: this rank, its device-side call counter and every
+// rank's exchange buffer (mapped into this process).
 struct ExchangeArgs {
-    uint32_t world = 1, rank = 0, epoch = 0;
+    uint32_t world = 1, rank = 0;
+    uint32_t *epoch = nullptr;
     float *base[bml::kMaxExchangeRanks] = {};
 };
 
@@ -917,7 +918,7 @@ BML_API bml_status bml_attn_noalloc_check(void *stream) {
 // ---------------------------------------------------------------------------
 struct bml_kvsplit {
     int32_t device = 0;
-    uint32_t rank = 0, world = 1, n_heads = 0, head_dim = 0, units = 0, epoch = 0;
+    uint32_t rank = 0, world = 1, n_heads = 0, head_dim = 0, units = 0;
     float *buf = nullptr;  // this rank's exchange buffer
     size_t bytes = 0;
     float *peer[bml::kMaxExchangeRanks] = {};  // every rank's buffer, mapped here
@@ -1007,14 +1008,12 @@ BML_API bml_status bml_attn_decode_kvsplit(bml_kvsplit *h, const bml_seq_desc *s
     ExchangeArgs xa;
     xa.world = h->world;
     xa.rank = h->rank;
-    if (++h->epoch == 0) h->epoch = 1;  // flags start at 0: an epoch is never 0
-    xa.epoch = h->epoch;
+    // the epoch lives on the device (the kernel advances it), so a call may
+    // be captured in a CUDA graph and replayed
+    xa.epoch = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(h->buf) + bml::exchange_epoch_offset(h->units));
     for (uint32_t r = 0; r < h->world; ++r) xa.base[r] = h->peer[r];
-    bml_status st = decode_impl(slice_host, 1, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev,
-                                nullptr, nullptr, nullptr, workspace, workspace_bytes, stream, bml::kModeFinal, fn,
-                                0, bml::kWaitNs, 0, &xa);
-    if (st != BML_OK) --h->epoch;  // nothing was launched
-    return st;
+    return decode_impl(slice_host, 1, n_heads, n_kv_heads, head_dim, kv_dtype, scale, q_dev, out_dev, nullptr, nullptr,
+                       nullptr, workspace, workspace_bytes, stream, bml::kModeFinal, fn, 0, bml::kWaitNs, 0, &xa);
 }
 
 BML_API bml_status bml_kvsplit_destroy(bml_kvsplit *h) {

@@ -28,13 +28,19 @@ constexpr int kMaxSeqsPerLaunch = 256;
 constexpr int kMaxExchangeRanks = 8;
 constexpr int kExchangeUnitFloats = 36;
 // Exchange buffer of a rank: data [2 call parities][kMaxExchangeRanks][units]
-// units of kExchangeUnitFloats, then flags [2][kMaxExchangeRanks][units] u32.
+// units of kExchangeUnitFloats, then flags [2][kMaxExchangeRanks][units] u32,
+// then the rank's call counter (u32; the epoch of its last call, 0 before
+// the first), kept on the device so that a launch captured in a CUDA graph
+// takes a new epoch at every replay.
 __host__ __device__ inline size_t exchange_data_floats(uint32_t units) {
     return 2ull * kMaxExchangeRanks * units * kExchangeUnitFloats;
 }
-inline size_t exchange_bytes(uint32_t units) {
+inline size_t exchange_epoch_offset(uint32_t units) {
     return exchange_data_floats(units) * 4 + 2ull * kMaxExchangeRanks * units * 4;
 }
+inline size_t exchange_bytes(uint32_t units) { return exchange_epoch_offset(units) + 16; }
+// The epoch a call takes after `last`: never 0 (flags start at 0).
+__host__ __device__ inline uint32_t exchange_next_epoch(uint32_t last) { return last + 1u == 0u ? 1u : last + 1u; }
 
 enum DecodeMode : int { kModeFinal = 0, kModePartial = 1 };
 
@@ -76,8 +82,11 @@ struct DecodeParams {
     // KV split over GPUs (x_world > 1; one sequence a launch): each merge
     // item is one exchange unit (q-head row, 32 head dims); its rank's (M, L,
     // O / L) goes to every rank's exchange buffer over peer memory, and the
-    // output is merged from all ranks' units in rank order
-    uint32_t x_world, x_rank, x_epoch, x_units;
+    // output is merged from all ranks' units in rank order.  x_epoch: this
+    // rank's call counter in its own exchange buffer; the launch's epoch is
+    // the next value, and the launch's last CTA stores it back.
+    uint32_t x_world, x_rank, x_units;
+    uint32_t *x_epoch;
     float *x_base[kMaxExchangeRanks];  // every rank's exchange buffer, mapped here
     DecodeSeq seqs[kMaxSeqsPerLaunch];
 };

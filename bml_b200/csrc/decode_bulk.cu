@@ -285,8 +285,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
 // One warp, one exchange unit (q-head row qh, dims [dim0, dim0 + 32)) of a
 // KV split over GPUs.  This rank's (M, L, O / L) -- lane l holds dim l --
 // goes to every rank's buffer slot [parity][this rank][unit] with plain
-// stores over peer memory, then a release store of the call's epoch into
-// that rank's flag for it.  Lane r waits (bounded by p.wait_ns) for rank
+// stores over peer memory, then a release store of the call's epoch (the
+// next value of this rank's device-side call counter) into that rank's flag
+// for it.  Lane r waits (bounded by p.wait_ns) for rank
 // r's flag in this rank's buffer; the ranks' units are then merged in rank
 // order (so all ranks write bit-identical outputs).  A slot is reused two
 // calls later: by then every rank has finished the call that read it (a
@@ -294,7 +295,10 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
 __device__ __noinline__ void exchange_store(const DecodeParams &p, uint32_t unit, uint32_t qh, uint32_t dim0,
                                             float M, float L, float O, int lane) {
     constexpr float NEG_INF = -INFINITY;
-    const uint32_t par = p.x_epoch & 1u, W = p.x_world;
+    // the counter changes only at the exit of this launch's last CTA, after
+    // every exchange of the launch: all CTAs read the same value here
+    const uint32_t epoch = exchange_next_epoch(__ldcg(p.x_epoch));
+    const uint32_t par = epoch & 1u, W = p.x_world;
     const size_t data = exchange_data_floats(p.x_units);
     const size_t mine = ((size_t)(par * kMaxExchangeRanks + p.x_rank) * p.x_units + unit) * kExchangeUnitFloats;
     const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -309,13 +313,13 @@ __device__ __noinline__ void exchange_store(const DecodeParams &p, uint32_t unit
     __threadfence_system();  // the unit reaches every rank before its flag
     __syncwarp();
     const size_t fl = (size_t)(par * kMaxExchangeRanks + p.x_rank) * p.x_units + unit;
-    if ((uint32_t)lane < W) st_release_sys(reinterpret_cast<uint32_t *>(p.x_base[lane] + data) + fl, p.x_epoch);
+    if ((uint32_t)lane < W) st_release_sys(reinterpret_cast<uint32_t *>(p.x_base[lane] + data) + fl, epoch);
     bool ok = true;
     if ((uint32_t)lane < W) {
         const uint32_t *flag = reinterpret_cast<const uint32_t *>(p.x_base[p.x_rank] + data) +
                                (size_t)(par * kMaxExchangeRanks + lane) * p.x_units + unit;
         uint64_t t0 = 0;
-        for (uint32_t polls = 0; ld_acquire_sys(flag) != p.x_epoch; ++polls) {
+        for (uint32_t polls = 0; ld_acquire_sys(flag) != epoch; ++polls) {
             const uint64_t now = globaltimer_ns();
             if (!t0) t0 = now;
             if (now - t0 > p.wait_ns) {
@@ -943,6 +947,7 @@ __global__ void __launch_bounds__(BCfg<D, G, NW>::THREADS, 1)
             p.sched[1] = 0u;
             p.sched[2] = 0u;
             p.sched[0] = 0u;
+            if (p.x_world > 1) *p.x_epoch = exchange_next_epoch(__ldcg(p.x_epoch));  // this call's epoch
             __threadfence();
         }
     }
@@ -1053,7 +1058,7 @@ cudaError_t launch_decode_bulk(const DecodeParams &p, bml_dtype dt, uint32_t hea
     // a KV split over GPUs: one sequence, items of one row x 32 dims
     if (p.x_world > 1 && (p.x_world > (uint32_t)kMaxExchangeRanks || p.x_rank >= p.x_world || p.n_seqs != 1 ||
                           p.mode != kModeFinal || DS * 32u != head_dim || wpr != NW || R != 1 ||
-                          p.x_units != p.n_heads * DS || p.x_epoch == 0))
+                          p.x_units != p.n_heads * DS || p.x_epoch == nullptr))
         return cudaErrorInvalidValue;
     // the home CTAs: contiguous ranges covering the grid, each home CTA's
     // static tile and part inside its sequence

@@ -359,7 +359,10 @@ bml_status bml_softmax_f32(const float *x_dev, uint32_t n_rows, uint32_t n,
  * (any host channel), bml_kvsplit_open.  All ranks must then call
  * bml_attn_decode_kvsplit the same number of times with the same shape;
  * a rank whose peers do not arrive within 2 s stops waiting and records
- * BML_E_TIMEOUT in the workspace's error word (bml_attn_workspace_check). */
+ * BML_E_TIMEOUT in the workspace's error word (bml_attn_workspace_check).
+ * The calls' exchange epochs are counted on the device (in the exchange
+ * buffer, advanced by each launch), so the calls may be captured in a CUDA
+ * graph and replayed, on every rank alike. */
 typedef struct bml_kvsplit bml_kvsplit;
 #define BML_KVSPLIT_HANDLE_BYTES 64
 

@@ -6,8 +6,9 @@ handles.  Each rank decodes its contiguous half of a seeded bf16 cache and
 swaps per-(q head, 32 dims) partials with the other over peer memory; both
 must then hold the oracle's single-pass attention over the whole sequence
 (decode tolerance 1e-4), bit-identical between the ranks, on three calls in
-a row (the exchange slots alternate between two parities).  Skipped with
-fewer than two GPUs."""
+a row (the exchange slots alternate between two parities) and on three
+replays of a CUDA graph holding two calls (the exchange's epoch is kept on
+the device).  Skipped with fewer than two GPUs."""
 import os
 import socket
 
@@ -54,6 +55,25 @@ def _rank(rank, world, port, q, k, v, ret):
             torch.cuda.synchronize(dev)
             outs.append(out.cpu().numpy().copy())
         ws.check()
+        # two calls captured in a CUDA graph and replayed: the exchange epoch
+        # lives on the device, so every replay takes fresh epochs
+        g = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(g, stream=cap):
+                o1 = step(qd, batch, ws, total_len=k.shape[0])
+                o2 = step(qd, batch, ws, total_len=k.shape[0])
+        torch.cuda.current_stream(dev).wait_stream(cap)
+        for _ in range(3):
+            o1.zero_()
+            o2.zero_()
+            g.replay()
+            torch.cuda.synchronize(dev)
+            outs.append(o1.cpu().numpy().copy())
+            outs.append(o2.cpu().numpy().copy())
+        ws.check()
+        del g
         step.close()
         ret[rank] = outs
     finally:
