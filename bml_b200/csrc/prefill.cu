@@ -202,6 +202,29 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t in_fmt, uint32_t m, u
     return (1u << 4) | (in_fmt << 7) | (in_fmt << 10) | (b_mn_major << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
 }
 
+// (2^e.x, 2^e.y) on the FMA pipe, for a share of the softmax's
+// exponentials (the SFU's exp2 runs at 16 a clock an SM, which is as long
+// per 128 x 128 tile as the tile's two MMAs).  Range reduction e = n + f,
+// n = round(e) by the 1.5 * 2^23 add, f in [-1/2, 1/2]; 2^f by a cubic
+// fitted here by reweighted least squares on Chebyshev nodes (maximum
+// relative error 7.7e-5 on [-1/2, 1/2], below bf16's 2^-8 rounding of p);
+// 2^n added to the exponent field as an integer.  Arguments below -120
+// (masked keys are -inf) give 2^-120 instead of 0: ~1e-36 of a row sum of
+// at least 1.
+__device__ __forceinline__ float2 exp2_poly_pair(float2 e) {
+    e.x = fmaxf(e.x, -120.f);
+    e.y = fmaxf(e.y, -120.f);
+    const float2 t = __fadd2_rn(e, make_float2(12582912.f, 12582912.f));  // low mantissa bits: round(e)
+    const float2 r = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+    const float2 f = __ffma2_rn(r, make_float2(-1.f, -1.f), e);            // e - round(e), exact
+    float2 q = __ffma2_rn(f, make_float2(0.055088736f, 0.055088736f), make_float2(0.24260406f, 0.24260406f));
+    q = __ffma2_rn(f, q, make_float2(0.69327623f, 0.69327623f));
+    q = __ffma2_rn(f, q, make_float2(0.99992895f, 0.99992895f));
+    q.x = __int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23));
+    q.y = __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23));
+    return q;
+}
+
 // two f32 -> one 32-bit word of 16-bit values, lo in the low half
 template <bool kF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
@@ -491,9 +514,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 
             // p = 2^(s*c - m), written as packed 16-bit pairs into columns
             // 0..63 of S_x (kv 2i, 2i+1 -> column i) and released to the MMA
-            // warp in two halves.  All exponentials run on the SFU: measured on
-            // B200, moving a share of them to a polynomial on the FMA pipe
-            // (exp2_poly2) costs more issue slots than it frees SFU time here.
+            // warp in two halves.  An eighth of the exponentials run on the FMA
+            // pipe (exp2_poly_pair), the rest on the SFU: measured on B200
+            // (4 x 8192 tokens, kernel alone), 2.002 ms with none, 1.910 with
+            // an eighth, 1.910-1.922 with 3/16, 1.926-1.957 with a quarter,
+            // 2.14 with 3/8 and 2.21 with half (issue slots run out).
             const float2 c2 = make_float2(c, c), nm2 = make_float2(-m_use, -m_use);
             float2 sum4[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                               make_float2(0.f, 0.f)};
@@ -506,8 +531,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
                     for (int i = 0; i < 32; i += 2) {
                         float2 e = __ffma2_rn(make_float2(sv[qc * 32 + i], sv[qc * 32 + i + 1]), c2, nm2);
-                        e.x = fast_exp2(e.x);
-                        e.y = fast_exp2(e.y);
+                        if (((i >> 1) & 7) == 7) {  // an eighth of the pairs on the FMA pipe
+                            e = exp2_poly_pair(e);
+                        } else {
+                            e.x = fast_exp2(e.x);
+                            e.y = fast_exp2(e.y);
+                        }
                         sum4[(i >> 1) & 3] = __fadd2_rn(sum4[(i >> 1) & 3], e);
                         w[i >> 1] = pack2<kF16>(e.x, e.y);
                     }
