@@ -32,7 +32,7 @@ class BmlInvalid(BmlError, ValueError):
 
 
 class BmlUnsupported(BmlError, NotImplementedError):
-    """BML_E_UNSUPPORTED: a valid shape this build has no kernel for."""
+    """BML_E_UNSUPPORTED: a valid shape this library has no kernel for."""
 
 
 class bml_kv_desc(C.Structure):

@@ -93,7 +93,7 @@ uint64_t element_size(uint32_t t) {
 bool is_quantized(uint32_t t) { return (t >= 2 && t <= 23) || t == 1 || t == 29; }
 
 // ggml block layouts: (values per block, bytes per block); (0, 0) where
-// this build does not know the layout.
+// this library does not know the layout.
 void block_layout(uint32_t t, uint64_t *vals, uint64_t *bytes) {
     static const struct { uint32_t t; uint64_t v, b; } tab[] = {
         {2, 32, 18}, {3, 32, 20}, {6, 32, 22}, {7, 32, 24}, {8, 32, 34}, {9, 32, 36},

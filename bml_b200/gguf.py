@@ -44,7 +44,7 @@ class TensorInfo:
     present: bool      # tensor_data() is Some
     data_offset: int   # absolute file offset of the data
     view_len: int      # bytes of tensor_data()'s slice
-    nbytes: int        # exact stored size (0: layout unknown to this build)
+    nbytes: int        # exact stored size (0: a layout this library does not know)
 
 
 def _text(ptr: int, n: int) -> str:

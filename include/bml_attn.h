@@ -50,7 +50,7 @@ typedef int32_t bml_status;
 #define BML_E_NCCL        3 /* reserved for communicator errors              */
 #define BML_E_TIMEOUT     4 /* a bounded device-side wait gave up            */
 #define BML_E_OOM         5 /* device allocation failed                      */
-#define BML_E_UNSUPPORTED 6 /* valid shape this build has no kernel for      */
+#define BML_E_UNSUPPORTED 6 /* valid shape the library has no kernel for    */
 
 typedef enum bml_dtype { BML_F32 = 0, BML_F16 = 1, BML_BF16 = 2 } bml_dtype;
 

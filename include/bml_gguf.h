@@ -76,7 +76,7 @@ typedef struct bml_gguf_tensor {
     int32_t present;
     uint64_t data_offset;
     uint64_t view_len;
-    /* Exact stored size from the type's block layout (0 where this build
+    /* Exact stored size from the type's block layout (0 where the library
      * does not know the type's layout); what bml_gguf_upload copies. */
     uint64_t nbytes;
 } bml_gguf_tensor;

@@ -61,7 +61,7 @@ def test_upload_refusals(cuda, model_file, tmp_path):
     p, tensors = model_file
     with gguf.GgufFile(p) as f:
         with pytest.raises(_lib.BmlUnsupported):
-            f.upload(["iq"])  # a block layout this build does not know
+            f.upload(["iq"])  # a block layout this library does not know
     # a tensor that runs past the end of the file
     raw = open(p, "rb").read()
     cut = tmp_path / "cut.gguf"

@@ -173,7 +173,8 @@ def test_golden_fixtures():
         np.testing.assert_array_equal(oracle.softmax_f32(g[f"softmax_in_{i}"]), g[f"softmax_out_{i}"])
 
 
-def test_batched_lengths_match_survey_sum():
+def test_batched_lengths_total_143173_positions():
+    """The 64 ragged lengths U[128, 4096] (seed 2) add up to 143,173 positions."""
     assert int(W.batched_lengths().sum()) == 143173
 
 
